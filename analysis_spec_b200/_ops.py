@@ -1,0 +1,277 @@
+"""Torch-tensor front end of the C ABI: shape/stride/device checks, then one
+libspeckv call on the current CUDA stream of the tensors' device.
+
+Every function here requires CUDA tensors and raises otherwise; there is no
+CPU path in the product.
+"""
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError('analysis_spec_b200 kernels need CUDA tensors; got a tensor on '
+                               f'{t.device} (the product has no CPU path)')
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _pool_geometry(pool):
+    if pool.dim() != 4 or pool.stride(3) != 1 or pool.stride(2) != pool.shape[3] or \
+            (pool.shape[1] > 1 and pool.stride(1) != pool.shape[2] * pool.shape[3]) or \
+            (pool.shape[0] > 1 and pool.stride(0) != pool.shape[1] * pool.shape[2] * pool.shape[3]):
+        raise ValueError('KV pools must be contiguous (batch_capacity, heads, capacity, dim) tensors')
+    return pool.shape
+
+
+def _chunks(n):
+    for start in range(0, n, _lib.MAX_LAYERS):
+        yield start, min(n, start + _lib.MAX_LAYERS)
+
+
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length):
+    """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers)."""
+    k0, v0 = key_srcs[0], value_srcs[0]
+    _require_cuda(key_pools[0], k0)
+    bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
+    batch, h, rows, d = k0.shape
+    if h != heads or d != dim or tuple(v0.shape) != tuple(k0.shape):
+        raise ValueError('appended K/V shape does not match the pool')
+    if batch > bcap:
+        raise ValueError('appended batch exceeds pool batch capacity')
+    if k0.stride(3) != 1 or v0.stride(3) != 1:
+        raise ValueError('appended K/V need unit stride on head_dim')
+    for srcs, first in ((key_srcs, k0), (value_srcs, v0)):
+        for t in srcs:
+            if t.shape != first.shape or t.stride() != first.stride() or t.dtype != key_pools[0].dtype:
+                raise ValueError('every layer must append K/V of one shape, stride and the pool dtype')
+    ks =_lib.i64_array(k0.stride()[:3])
+    vs = _lib.i64_array(v0.stride()[:3])
+    es = key_pools[0].element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_append_rows', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]),
+                  _lib.ptr_array([s.data_ptr() for s in key_srcs[a:b]]),
+                  _lib.ptr_array([s.data_ptr() for s in value_srcs[a:b]]),
+                  b - a, batch, heads, rows, dim, capacity, length, ks, vs, es, _stream(k0))
+
+
+def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width):
+    """Accepted-suffix compaction of every layer (one launch per 64 layers)."""
+    _require_cuda(key_pools[0], chosen)
+    _, heads, capacity, dim = _pool_geometry(key_pools[0])
+    if chosen.dtype != torch.long or chosen.dim() != 2:
+        raise ValueError('chosen indices must be a (batch, width) int64 tensor')
+    if chosen.shape[0] < batch or chosen.shape[1] < width or batch > key_pools[0].shape[0]:
+        raise ValueError('chosen indices do not cover the live batch / width')
+    es = key_pools[0].element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_compact_suffix', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim,
+                  capacity, length, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, extension, width,
+                  es, _stream(chosen))
+
+
+def remap_scratch_elements(new_batch, heads, dim, length, element_size):
+    """Elements of pool dtype the remap needs as scratch (0 for the single on-chip pass)."""
+    nbytes = _lib.load().speckv_remap_scratch_bytes(new_batch, heads, dim, length, element_size)
+    return (nbytes + element_size - 1) // element_size
+
+
+def remap_rows(key_pools, value_pools, indices, length, scratch=None):
+    """pool[:n] = pool[indices] over [0, length) for every layer."""
+    _require_cuda(key_pools[0], indices)
+    bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
+    if indices.dtype != torch.long or not indices.is_contiguous():
+        indices = indices.to(torch.long).contiguous()
+    es = key_pools[0].element_size()
+    scratch_bytes = 0 if scratch is None else scratch.numel() * scratch.element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_remap_rows', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, indices.data_ptr(),
+                  indices.numel(), bcap, heads, dim, capacity, length, _ptr(scratch), scratch_bytes, es,
+                  _stream(indices))
+
+
+def move_rows(key_pools, value_pools, sources, destinations, length):
+    """pool[destinations[j]] = pool[sources[j]] over [0, length) for every layer."""
+    _require_cuda(key_pools[0], sources, destinations)
+    bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
+    sources = sources.to(torch.long).contiguous()
+    destinations = destinations.to(torch.long).contiguous()
+    if sources.numel() != destinations.numel():
+        raise ValueError('sources and destinations differ in length')
+    es = key_pools[0].element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_move_rows', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, sources.data_ptr(),
+                  destinations.data_ptr(), sources.numel(), bcap, heads, dim, capacity, length, es,
+                  _stream(sources))
+
+
+def _contig_long(name, t):
+    if t.dtype != torch.long:
+        raise ValueError(f'{name} must be int64')
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def pack_tree(full_parents, full_contexts, all_tokens, chosen, out_parents, out_tokens, out_contexts):
+    _require_cuda(full_parents, full_contexts, all_tokens, chosen, out_parents, out_tokens, out_contexts)
+    batch, full_count = full_parents.shape
+    packed = chosen.shape[1]
+    full_parents, full_contexts, all_tokens, chosen = (_contig_long(n, t) for n, t in (
+        ('full_parents', full_parents), ('full_contexts', full_contexts), ('all_tokens', all_tokens),
+        ('chosen', chosen)))
+    if all_tokens.shape[1] != full_count or full_contexts.shape[1] != full_count:
+        raise ValueError('full tree tensors differ in node count')
+    for t in (out_parents, out_tokens, out_contexts):
+        if t.shape != (batch, packed + 1) or t.stride() != out_parents.stride() or t.stride(1) != 1:
+            raise ValueError('packed outputs must be (batch, packed + 1) with unit column stride')
+    _lib.call('speckv_pack_tree', full_parents.data_ptr(), full_contexts.data_ptr(), all_tokens.data_ptr(),
+              chosen.data_ptr(), batch, full_count, packed, out_parents.data_ptr(), out_tokens.data_ptr(),
+              out_contexts.data_ptr(), out_parents.stride(0), _stream(chosen))
+
+
+def trace_path(parents, tokens, contexts, samples, eos, out_tokens, out_indices, out_contexts, lengths):
+    _require_cuda(parents, tokens, contexts, samples, out_tokens, out_indices, out_contexts, lengths)
+    batch, rows = samples.shape
+    parents, tokens, contexts, samples = (_contig_long(n, t) for n, t in
+                                          (('parents', parents), ('tokens', tokens), ('contexts', contexts),
+                                           ('samples', samples)))
+    if out_tokens.stride() != out_indices.stride() or out_tokens.stride() != out_contexts.stride():
+        raise ValueError('trace outputs must share strides')
+    if lengths.stride(0) != 1 and lengths.numel() > 1:
+        raise ValueError('lengths must be contiguous')
+    _lib.call('speckv_trace_path', parents.data_ptr(), tokens.data_ptr(), contexts.data_ptr(), samples.data_ptr(),
+              batch, rows, int(eos), out_tokens.data_ptr(), out_indices.data_ptr(), out_contexts.data_ptr(),
+              out_tokens.stride(0), out_tokens.stride(1), out_tokens.shape[1], lengths.data_ptr(),
+              _stream(samples))
+
+
+def _check_pad_outputs(tokens, indices, mask):
+    if tokens.stride() != indices.stride() or tokens.stride() != mask.stride():
+        raise ValueError('padded outputs must share strides')
+    if tokens.dtype != torch.long or indices.dtype != torch.long or mask.dtype != torch.bool:
+        raise ValueError('padded outputs must be int64, int64, bool')
+
+
+def pad_verified_path(path_tokens, path_indices, lengths, width, past, eos, tokens, indices, mask, last):
+    _require_cuda(path_tokens, path_indices, lengths, tokens, indices, mask, last)
+    _check_pad_outputs(tokens, indices, mask)
+    batch, capacity = path_tokens.shape
+    lengths = _contig_long('lengths', lengths)
+    _lib.call('speckv_pad_verified_path', path_tokens.data_ptr(), path_tokens.stride(0), path_tokens.stride(1),
+              path_indices.data_ptr(), path_indices.stride(0), path_indices.stride(1), lengths.data_ptr(), batch,
+              capacity, int(width), int(past), int(eos), tokens.data_ptr(), indices.data_ptr(), mask.data_ptr(),
+              tokens.stride(0), tokens.stride(1), last.data_ptr(), last.stride(0), _stream(path_tokens))
+
+
+def pad_schedule(path_tokens, path_indices, lengths, past, eos, tokens, indices, mask, last, packet,
+                 snapshot=None):
+    _require_cuda(path_tokens, path_indices, lengths, tokens, indices, mask, last, packet, snapshot)
+    _check_pad_outputs(tokens, indices, mask)
+    batch, capacity = path_tokens.shape
+    lengths = _contig_long('lengths', lengths)
+    if packet.shape[1] < capacity + 3:
+        raise ValueError('packet too narrow for the path capacity')
+    if snapshot is not None:
+        # The snapshot lands in column capacity + 3, just past a (b, capacity + 3)
+        # slice of the caller's (b, capacity + 4) packet: check the storage holds it.
+        last_elem = packet.storage_offset() + (batch - 1) * packet.stride(0) + (capacity + 3) * packet.stride(1)
+        if last_elem >= packet.untyped_storage().nbytes() // packet.element_size():
+            raise ValueError('packet storage has no snapshot column')
+    _lib.call('speckv_pad_schedule', path_tokens.data_ptr(), path_tokens.stride(0), path_tokens.stride(1),
+              path_indices.data_ptr(), path_indices.stride(0), path_indices.stride(1), lengths.data_ptr(), batch,
+              capacity, int(past), int(eos), tokens.data_ptr(), indices.data_ptr(), mask.data_ptr(),
+              tokens.stride(0), tokens.stride(1), last.data_ptr(), last.stride(0), packet.data_ptr(),
+              packet.stride(0), packet.stride(1), _ptr(snapshot), _stream(path_tokens))
+
+
+def tree_mask(parents, past, steps, mask, pad=None):
+    """Dense additive ancestor mask (batch, 1, rows, past + rows); `pad` (batch, >= cols) bool forces columns off."""
+    _require_cuda(parents, mask, pad)
+    batch, rows = parents.shape
+    parents = _contig_long('parents', parents)
+    if not mask.is_contiguous() or tuple(mask.shape) != (batch, 1, rows, past + rows):
+        raise ValueError('mask must be a contiguous (batch, 1, rows, past + rows) tensor')
+    if mask.dtype not in _DTYPE_CODE:
+        raise ValueError(f'unsupported mask dtype {mask.dtype}')
+    pad_stride = 0
+    if pad is not None:
+        if pad.dtype != torch.bool or pad.stride(-1) != 1 or pad.shape[-1] < past + rows:
+            raise ValueError('pad must be a bool (batch, columns) tensor covering past + rows columns')
+        pad_stride = pad.stride(0)
+    _lib.call('speckv_tree_mask', parents.data_ptr(), batch, rows, int(past), int(steps), mask.data_ptr(),
+              _DTYPE_CODE[mask.dtype], _ptr(pad), pad_stride, _stream(parents))
+
+
+def position_update(newly_padded, past, positions, past_positions, pad_rows=None, owners=None, pad_live=None):
+    _require_cuda(newly_padded, positions, past_positions, pad_rows, owners, pad_live)
+    batch, width = newly_padded.shape
+    if newly_padded.stride(1) != 1 or positions.stride(1) != 1:
+        raise ValueError('newly_padded / positions need unit column stride')
+    if past_positions.dtype != torch.long or positions.dtype != torch.long or not past_positions.is_contiguous():
+        raise ValueError('positions must be contiguous int64')
+    if owners is not None:
+        owners = _contig_long('owners', owners)
+    _lib.call('speckv_position_update', _ptr(pad_rows), 0 if pad_rows is None else pad_rows.stride(0),
+              0 if pad_rows is None else pad_rows.shape[0], _ptr(owners), _ptr(pad_live),
+              0 if pad_live is None else pad_live.stride(0), newly_padded.data_ptr(), newly_padded.stride(0), batch,
+              int(past), width, positions.data_ptr(), positions.stride(0), past_positions.data_ptr(),
+              _stream(newly_padded))
+
+
+def tree_attention(query, key, value, mask, scale, out=None):
+    """GQA attention (batch, Hq, R, D) x (batch, Hkv, L, D) -> (batch, R, Hq, D) with an additive mask."""
+    _require_cuda(query, key, value, mask)
+    batch, q_heads, rows, dim = query.shape
+    kv_heads, kv_len = key.shape[1], key.shape[2]
+    if query.dtype not in _DTYPE_CODE or key.dtype != query.dtype or value.dtype != query.dtype:
+        raise ValueError('query/key/value must share a float dtype')
+    if query.stride(3) != 1 or key.stride(3) != 1 or value.stride(3) != 1:
+        raise ValueError('query/key/value need unit stride on head_dim')
+    if tuple(value.shape) != tuple(key.shape) or key.shape[0] != batch or key.shape[3] != dim:
+        raise ValueError('key/value shapes do not match the query')
+    mask_code = 0
+    if mask is not None:
+        if mask.dim() != 4 or mask.shape[1] != 1 or mask.shape[0] != batch or mask.shape[2] != rows or \
+                mask.shape[3] != kv_len:
+            mask = mask.expand(batch, 1, rows, kv_len)
+        if mask.dtype == torch.bool:
+            mask = torch.zeros((), dtype=query.dtype, device=mask.device).masked_fill(
+                ~mask, torch.finfo(query.dtype).min).expand(batch, 1, rows, kv_len)
+        mask = mask.contiguous()
+        mask_code = _DTYPE_CODE[mask.dtype]
+    if out is None:
+        out = torch.empty((batch, rows, q_heads, dim), device=query.device, dtype=query.dtype)
+    _lib.call('speckv_tree_attention', query.data_ptr(), _lib.i64_array(query.stride()[:3]), key.data_ptr(),
+              _lib.i64_array(key.stride()[:3]), value.data_ptr(), _lib.i64_array(value.stride()[:3]), _ptr(mask),
+              mask_code, out.data_ptr(), batch, q_heads, kv_heads, rows, kv_len, dim, float(scale),
+              _DTYPE_CODE[query.dtype], _stream(query))
+    return out
+
+
+def device_error(device=None):
+    """Reads and clears the library's device error word; returns (kind, value) or None."""
+    import ctypes
+    word = ctypes.c_uint64(0)
+    dev = torch.device('cuda', torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _lib.call('speckv_device_error', ctypes.byref(word), torch.cuda.current_stream(dev).cuda_stream)
+    if word.value == 0:
+        return None
+    kind = word.value >> 48
+    value = word.value & 0xFFFFFFFFFFFF
+    if value >> 47:
+        value -= 1 << 48
+    return _lib.DEVICE_ERROR_KINDS.get(kind, str(kind)), value

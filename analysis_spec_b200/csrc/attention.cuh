@@ -1,0 +1,24 @@
+// Argument block shared by the tree-verify attention paths.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace speckv {
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* mask;  // (batch, 1, rows, kv_len) contiguous, or null
+  void* out;         // (batch, rows, q_heads, dim) contiguous
+  long long qs[3], ks[3], vs[3];  // element strides (b, h, t); dim stride is 1
+  long long batch, q_heads, kv_heads, rows, kv_len, dim;
+  float scale;
+  int dtype, mask_dtype;
+};
+
+// CUDA-core path (any head dim <= 256, any dtype).
+int attention_generic(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace speckv

@@ -1,0 +1,439 @@
+"""Preallocated, geometrically growing static KV cache behind the HF ``Cache`` API.
+
+Drop-in for ``helper/opd_static_cache.py`` of the reference: same classes,
+methods, attributes, counters and error messages. Each layer keeps its own K
+and V pool ``(batch_capacity, heads, capacity, head_dim)``; the visible cache is
+the strided view ``pool[:batch_size, :, :length]``.
+
+All row movement runs in libspeckv's sm_100a kernels. Cache-wide operations
+(repeat / select / swap-remove, and the B200 additions ``update_layers`` and
+``commit_accepted``) move every layer, K and V, in ONE launch instead of the
+reference's per-layer launches.
+
+Reference semantics followed (file:line in the reference project):
+  StaticAppendLayer            helper/opd_static_cache.py:17-174
+  OPDStaticCache               helper/opd_static_cache.py:177-244
+  swap_remove_plan             helper/opd_static_cache.py:247-254
+  persistent_cache             helper/opd_static_cache.py:257-264
+"""
+import weakref
+
+import torch
+from transformers.cache_utils import Cache
+
+try:
+    from transformers.cache_utils import CacheLayerMixin
+except ImportError:  # older transformers
+    CacheLayerMixin = object
+
+from . import _ops
+
+LAYER_COUNTERS = ('pool_allocations', 'full_kv_reallocations', 'full_history_copies', 'full_history_copy_bytes',
+                  'row_compactions', 'row_compaction_bytes')
+
+
+class StaticAppendLayer(CacheLayerMixin):
+    """One layer's K/V pools with suffix append, crop, remap and swap-remove."""
+
+    is_compileable = False
+    is_sliding = False
+
+    def __init__(self, capacity, owner=None):
+        self.key_pool = self.value_pool = None
+        self.length = self.batch_size = self.batch_capacity = 0
+        # Weak link: the cache owns its layers; a strong back-reference would keep
+        # every pool alive until a cyclic GC pass after the rollout.
+        self._owner_ref = weakref.ref(owner) if owner is not None else None
+        self.stats = {name: 0 for name in LAYER_COUNTERS}
+        super().__init__()
+        self.capacity = capacity
+        self.is_initialized = False
+
+    # ---- views ---------------------------------------------------------------
+    @property
+    def owner(self):
+        return self._owner_ref() if self._owner_ref is not None else None
+
+    @property
+    def keys(self):
+        return None if self.key_pool is None else self.key_pool[:self.batch_size, :, :self.length, :]
+
+    @keys.setter
+    def keys(self, value):
+        if value is not None:
+            self._adopt_view(value, self.key_pool)
+
+    @property
+    def values(self):
+        return None if self.value_pool is None else self.value_pool[:self.batch_size, :, :self.length, :]
+
+    @values.setter
+    def values(self, value):
+        if value is not None:
+            self._adopt_view(value, self.value_pool)
+
+    def _adopt_view(self, view, pool):
+        # Only views of this layer's own storage may be assigned back (they set
+        # the visible length / batch); anything else would silently detach the pool.
+        if pool is None:
+            raise RuntimeError('cache assignment before initialization')
+        if view.untyped_storage().data_ptr() != pool.untyped_storage().data_ptr():
+            raise RuntimeError('use batch_select_indices for row remap; external KV replacement is unsupported')
+        self.length, self.batch_size = view.shape[-2], view.shape[0]
+
+    # ---- allocation ----------------------------------------------------------
+    def _chunk(self):
+        owner = self.owner
+        return owner.chunk_size if owner is not None else 256
+
+    def _capacity_for(self, needed):
+        chunk = self._chunk()
+        return max(self.capacity, -(-needed // chunk) * chunk)
+
+    def lazy_initialization(self, key_states, value_states):
+        self.dtype, self.device = key_states.dtype, key_states.device
+        self.batch_size = key_states.shape[0]
+        owner = self.owner
+        self.batch_capacity = max(self.batch_size, owner.batch_capacity if owner is not None else 0)
+        self.capacity = self._capacity_for(key_states.shape[-2])
+        shape = (self.batch_capacity, key_states.shape[1], self.capacity, key_states.shape[-1])
+        self.key_pool = torch.empty(shape, dtype=key_states.dtype, device=key_states.device)
+        self.value_pool = torch.empty(shape, dtype=value_states.dtype, device=value_states.device)
+        self.stats['pool_allocations'] += 1
+        self.is_initialized = True
+
+    def _grow(self, needed, batch_needed=None):
+        """Replace the pools when `needed` positions or `batch_needed` rows do not fit.
+
+        Capacity at least doubles (rounded up to the chunk); the live history
+        [:batch_size, :, :length] is copied into the new pools.
+        """
+        batch_needed = self.batch_size if batch_needed is None else batch_needed
+        if needed <= self.capacity and batch_needed <= self.batch_capacity:
+            return
+        capacity = self._capacity_for(max(needed, 2 * self.capacity)) if needed > self.capacity else self.capacity
+        rows = max(batch_needed, self.batch_capacity)
+        shape = (rows, self.key_pool.shape[1], capacity, self.key_pool.shape[-1])
+        old_keys, old_values = self.keys, self.values
+        keys = torch.empty(shape, dtype=self.key_pool.dtype, device=self.key_pool.device)
+        values = torch.empty(shape, dtype=self.value_pool.dtype, device=self.value_pool.device)
+        if self.length and self.batch_size:
+            _ops.append_rows([keys], [values], [old_keys], [old_values], 0)
+        self.stats['pool_allocations'] += 1
+        self.stats['full_kv_reallocations'] += 1
+        if self.length:
+            self.stats['full_history_copies'] += 1
+            self.stats['full_history_copy_bytes'] += (old_keys.numel() * old_keys.element_size() +
+                                                      old_values.numel() * old_values.element_size())
+        self.key_pool, self.value_pool = keys, values
+        self.capacity, self.batch_capacity = capacity, rows
+
+    # ---- append ----------------------------------------------------------------
+    def _prepare_append(self, key_states, value_states):
+        if not self.is_initialized:
+            self.lazy_initialization(key_states, value_states)
+        if key_states.shape[0] != self.batch_size:
+            raise ValueError('KV batch differs from live request count')
+        end = self.length + key_states.shape[-2]
+        self._grow(end)
+        if key_states.dtype != self.key_pool.dtype:
+            key_states = key_states.to(self.key_pool.dtype)
+        if value_states.dtype != self.value_pool.dtype:
+            value_states = value_states.to(self.value_pool.dtype)
+        return key_states, value_states, end
+
+    def update(self, key_states, value_states, *args, **kwargs):
+        key_states, value_states, end = self._prepare_append(key_states, value_states)
+        _ops.append_rows([self.key_pool], [self.value_pool], [key_states], [value_states], self.length)
+        self.length = end
+        return self.keys, self.values
+
+    def get_seq_length(self):
+        return self.length
+
+    def get_max_cache_shape(self):
+        return self.capacity
+
+    def get_max_length(self):
+        return self.capacity
+
+    def get_mask_sizes(self, query_length):
+        return self.length + query_length, 0
+
+    def crop(self, length):
+        target = length if length >= 0 else self.length + length
+        self.length = max(0, min(self.length, target))
+
+    def reset(self):
+        self.length = 0
+
+    # ---- remap / release -------------------------------------------------------
+    def _count_select(self, new_batch):
+        self.stats['row_compactions'] += 1
+        moved = new_batch * self.key_pool.shape[1] * self.length * self.key_pool.shape[-1] * (
+            self.key_pool.element_size() + self.value_pool.element_size())
+        self.stats['row_compaction_bytes'] += moved
+        if moved:
+            self.stats['full_history_copies'] += 1
+            self.stats['full_history_copy_bytes'] += moved
+        self.batch_size = new_batch
+
+    def _remap_scratch(self, new_batch):
+        elements = _ops.remap_scratch_elements(new_batch, self.key_pool.shape[1], self.key_pool.shape[-1],
+                                               self.length, self.key_pool.element_size())
+        if not elements:
+            return None
+        owner = self.owner
+        key = ('cuda_live', self.key_pool.dtype, self.key_pool.device)
+        scratch = owner._scratch.get(key) if owner is not None else None
+        if scratch is None or scratch.numel() < elements:
+            scratch = torch.empty(1 << max(0, (elements - 1).bit_length()), dtype=self.key_pool.dtype,
+                                  device=self.key_pool.device)
+            if owner is not None:
+                owner._scratch[key] = scratch
+        return scratch
+
+    def batch_select_indices(self, indices):
+        new_batch = indices.numel()
+        self._grow(self.length, new_batch)
+        _ops.remap_rows([self.key_pool], [self.value_pool], indices, self.length, self._remap_scratch(new_batch))
+        self._count_select(new_batch)
+
+    def batch_repeat_interleave(self, repeats):
+        if repeats < 1:
+            raise ValueError('positive repeats required')
+        if repeats != 1:
+            self.batch_select_indices(_repeat_indices(self.batch_size, repeats, self.key_pool.device))
+
+    def _count_swap(self, new_batch, count):
+        moved = count * self.key_pool.shape[1] * self.length * self.key_pool.shape[-1] * (
+            self.key_pool.element_size() + self.value_pool.element_size())
+        self.stats['row_compactions'] += 1
+        self.stats['row_compaction_bytes'] += moved
+        self.stats['full_history_copy_bytes'] += moved
+        if moved:
+            self.stats['full_history_copies'] += 1
+        self.batch_size = new_batch
+
+    def swap_remove(self, new_batch, sources, destinations):
+        """Moves disjoint live tail rows into holes below new_batch; survivors stay put."""
+        count = sources.numel()
+        if count and self.length:
+            _ops.move_rows([self.key_pool], [self.value_pool], sources, destinations, self.length)
+        self._count_swap(new_batch, count)
+
+
+def _repeat_indices(batch, repeats, device):
+    return torch.arange(batch, device=device).repeat_interleave(repeats)
+
+
+def _uniform(layers):
+    """True when every layer's pools share shape and dtype (one launch can cover them)."""
+    first = layers[0]
+    return all(layer.key_pool is not None and layer.key_pool.shape == first.key_pool.shape and
+               layer.key_pool.dtype == first.key_pool.dtype and layer.value_pool.dtype == first.key_pool.dtype and
+               layer.length == first.length and layer.batch_size == first.batch_size for layer in layers)
+
+
+class OPDStaticCache(Cache):
+    """HF ``Cache`` whose layers are StaticAppendLayer pools kept across rollouts."""
+
+    def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256):
+        if capacity < 1 or chunk_size < 1 or batch_capacity < 0:
+            raise ValueError('positive KV capacity/chunk and nonnegative batch capacity required')
+        try:
+            super().__init__(layers=[])
+        except TypeError:
+            super().__init__()
+            self.layers = []
+        self.capacity, self.batch_capacity, self.chunk_size = capacity, batch_capacity, chunk_size
+        self._scratch = {}
+        self.kv_rows_moved = 0
+
+    # ---- rollout lifetime ------------------------------------------------------
+    def begin_rollout(self, batch, batch_capacity):
+        self.batch_capacity = max(self.batch_capacity, batch_capacity)
+        self.kv_rows_moved = 0
+        for layer in self.layers:
+            layer.length = 0
+            layer.batch_size = batch
+            for key in layer.stats:
+                layer.stats[key] = 0
+
+    def end_rollout(self, max_retained_tokens=0):
+        for layer in self.layers:
+            layer.length = layer.batch_size = 0
+        if max_retained_tokens and any(layer.capacity > max_retained_tokens for layer in self.layers):
+            self.layers.clear()
+            self._scratch.clear()
+
+    def scratch(self, pool, shape):
+        """Reusable (rows, heads, chunk, dim) tile buffer keyed by device/dtype/geometry."""
+        rows = shape[0]
+        key = (pool.device, pool.dtype, shape[1], shape[-1])
+        buf = self._scratch.get(key)
+        if buf is None or any(a < b for a, b in zip(buf.shape, shape)):
+            full = (max(shape[0], self.batch_capacity), shape[1], self.chunk_size, shape[-1])
+            buf = torch.empty(full, dtype=pool.dtype, device=pool.device)
+            self._scratch[key] = buf
+        return buf[:rows]
+
+    # ---- HF cache protocol -----------------------------------------------------
+    def _layer(self, layer_idx):
+        while len(self.layers) <= layer_idx:
+            self.layers.append(StaticAppendLayer(self.capacity, self))
+        return self.layers[layer_idx]
+
+    def update(self, key_states, value_states, layer_idx, *args, **kwargs):
+        return self._layer(layer_idx).update(key_states, value_states)
+
+    def get_seq_length(self, layer_idx=0):
+        return self.layers[layer_idx].length if layer_idx < len(self.layers) else 0
+
+    def get_mask_sizes(self, query_length, layer_idx=0):
+        return self.get_seq_length(layer_idx) + query_length, 0
+
+    def get_max_cache_shape(self, layer_idx=0):
+        return self.layers[layer_idx].capacity if layer_idx < len(self.layers) else self.capacity
+
+    def crop(self, length):
+        for layer in self.layers:
+            layer.crop(length)
+
+    def __getitem__(self, index):
+        return self.layers[index].keys, self.layers[index].values
+
+    def __iter__(self):
+        for layer in self.layers:
+            yield layer.keys, layer.values
+
+    def __len__(self):
+        return len(self.layers)
+
+    def __bool__(self):
+        return bool(self.layers) and self.get_seq_length() > 0
+
+    # ---- cache-wide row movement (one launch for all layers) --------------------
+    def _select_all(self, indices):
+        layers = self.layers
+        if not layers:
+            return
+        new_batch = indices.numel()
+        for layer in layers:
+            layer._grow(layer.length, new_batch)
+        if _uniform(layers):
+            first = layers[0]
+            _ops.remap_rows([l.key_pool for l in layers], [l.value_pool for l in layers], indices, first.length,
+                            first._remap_scratch(new_batch))
+            for layer in layers:
+                layer._count_select(new_batch)
+        else:
+            for layer in layers:
+                _ops.remap_rows([layer.key_pool], [layer.value_pool], indices, layer.length,
+                                layer._remap_scratch(new_batch))
+                layer._count_select(new_batch)
+
+    def batch_repeat_interleave(self, repeats):
+        if repeats < 1:
+            raise ValueError('positive repeats required')
+        if repeats != 1 and self.layers:
+            first = self.layers[0]
+            self._select_all(_repeat_indices(first.batch_size, repeats, first.key_pool.device))
+        # Prefill repeat is excluded from kv_rows_moved, as in the reference.
+
+    def batch_select_indices(self, indices):
+        self._select_all(indices)
+        self.kv_rows_moved += indices.numel()
+
+    def swap_remove(self, new_batch, sources, destinations):
+        layers = self.layers
+        count = sources.numel()
+        if layers and count:
+            live = [l for l in layers if l.length]
+            if live and _uniform(live):
+                _ops.move_rows([l.key_pool for l in live], [l.value_pool for l in live], sources, destinations,
+                               live[0].length)
+            else:
+                for layer in live:
+                    _ops.move_rows([layer.key_pool], [layer.value_pool], sources, destinations, layer.length)
+        for layer in layers:
+            layer._count_swap(new_batch, count)
+        self.kv_rows_moved += count
+
+    # ---- B200 additions ----------------------------------------------------------
+    def update_layers(self, key_states, value_states):
+        """Appends key_states[l] / value_states[l] to layer l for every l in one launch.
+
+        Same result as calling ``update(key_states[l], value_states[l], l)`` for each
+        layer; returns the per-layer (keys, values) views.
+        """
+        if len(key_states) != len(value_states):
+            raise ValueError('one key and one value tensor per layer required')
+        prepared = []
+        for idx, (k, v) in enumerate(zip(key_states, value_states)):
+            prepared.append(self._layer(idx)._prepare_append(k, v))
+        layers = self.layers[:len(prepared)]
+        if _uniform(layers):
+            _ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers],
+                             [p[0] for p in prepared], [p[1] for p in prepared], layers[0].length)
+        else:
+            for layer, (k, v, _) in zip(layers, prepared):
+                _ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length)
+        for layer, (_, _, end) in zip(layers, prepared):
+            layer.length = end
+        return [(l.keys, l.values) for l in layers]
+
+    def commit_accepted(self, chosen, past, extension):
+        """Accepted-path commit of every layer in one launch, then crop.
+
+        Equivalent to ``compact_suffix_inplace`` on each layer's views followed by
+        ``crop(past + chosen.shape[1])`` (helper/opd_generate.py:632-643).
+        """
+        width = chosen.shape[1]
+        layers = self.layers
+        if layers and extension != width:
+            if _uniform(layers):
+                first = layers[0]
+                _ops.compact_suffix([l.key_pool for l in layers], [l.value_pool for l in layers],
+                                    first.batch_size, first.length, chosen, past, extension, width)
+            else:
+                for layer in layers:
+                    _ops.compact_suffix([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length,
+                                        chosen, past, extension, width)
+        self.crop(past + width)
+
+    def statistics(self):
+        totals = {name: sum(layer.stats[name] for layer in self.layers) for name in LAYER_COUNTERS}
+        totals['kv_cache_bytes'] = sum(pool.numel() * pool.element_size() for layer in self.layers
+                                       for pool in (layer.key_pool, layer.value_pool) if pool is not None)
+        totals['kv_compaction_workspace_bytes'] = sum(x.numel() * x.element_size() for x in self._scratch.values())
+        totals['kv_rows_moved'] = self.kv_rows_moved
+        totals['kv_history_copy_bytes'] = totals['full_history_copy_bytes']
+        return totals
+
+
+def swap_remove_plan(finished):
+    """Host plan for releasing finished rows: (keep, tail sources, hole destinations).
+
+    Holes are finished rows below the new batch size; they are filled, in order,
+    from the live rows above it taken from the end.
+    """
+    new_batch = len(finished) - sum(bool(x) for x in finished)
+    holes = [i for i in range(new_batch) if finished[i]]
+    tail = [i for i in range(len(finished) - 1, new_batch - 1, -1) if not finished[i]]
+    keep = list(range(new_batch))
+    for destination, source in zip(holes, tail):
+        keep[destination] = source
+    return keep, tail, holes
+
+
+def persistent_cache(model, name, batch, responses, device, dtype):
+    """Returns the model-owned cache `name`, re-created when device/dtype change."""
+    cache = getattr(model, name, None)
+    signature = (str(device), dtype)
+    if cache is None or getattr(cache, 'runtime_signature', None) != signature:
+        cache = OPDStaticCache(256, batch_capacity=batch * responses)
+        cache.runtime_signature = signature
+        setattr(model, name, cache)
+    cache.begin_rollout(batch, batch * responses)
+    return cache

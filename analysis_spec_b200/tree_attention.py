@@ -1,0 +1,43 @@
+"""Tree-verify GQA attention as a transformers ``AttentionInterface`` function.
+
+Replaces ``sdpa_attention_forward`` (transformers
+``integrations/sdpa_attention.py:40-104``) on the verify forward of
+``Qwen2Attention`` (``models/qwen2/modeling_qwen2.py:206-240``). With a 4-D
+mask, transformers' SDPA path disables its GQA mode and materialises
+``repeat_kv`` copies of K/V for every query head (``sdpa_attention.py:28-37,
+56-62``); this kernel reads each KV head of the strided cache views once for
+all query heads that share it and applies the additive mask in-kernel.
+
+Use: ``register()`` then ``model.config._attn_implementation = 'speckv_tree'``
+(or call ``tree_verify_attention`` directly).
+"""
+from . import _ops
+
+ATTENTION_NAME = 'speckv_tree'
+
+
+def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, is_causal=None,
+                          **kwargs):
+    """(module, q (B,Hq,R,D), k/v (B,Hkv,L,D), additive mask (B,1,R,L)) -> (out (B,R,Hq,D), None)."""
+    if dropout:
+        raise ValueError('tree_verify_attention is an inference kernel (dropout must be 0)')
+    scale = scaling if scaling is not None else query.shape[-1] ** -0.5
+    mask = attention_mask
+    if mask is not None and mask.shape[-1] > key.shape[-2]:
+        mask = mask[:, :, :, :key.shape[-2]]
+    causal = is_causal if is_causal is not None else getattr(module, 'is_causal', True)
+    if mask is None and causal and query.shape[2] > 1:
+        raise ValueError('tree_verify_attention needs an explicit mask for multi-query causal attention')
+    return _ops.tree_attention(query, key, value, mask, scale), None
+
+
+def register(name=ATTENTION_NAME):
+    """Registers the kernel with transformers' global attention (and mask) interfaces."""
+    from transformers import AttentionInterface
+    AttentionInterface.register(name, tree_verify_attention)
+    try:
+        from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS, sdpa_mask
+        ALL_MASK_ATTENTION_FUNCTIONS.register(name, sdpa_mask)
+    except ImportError:
+        pass
+    return name

@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Verify-round benchmark of the static-KV-cache / tree-verify path on B200.
+
+One step = one verify round of the Qwen2.5-3B geometry workload (36 layers,
+batch 64, 16 query / 2 KV heads x 128, bf16, max_len 4096, prefixes U{256..2048}
+left-padded to one shared length, 60-node trees of depth 6 / top-k 10, accepted
+length ~ geometric(mean 3.5) capped at 7):
+
+  tree mask (+ padding)  -> append the 61 tree rows of all 36 layers (one launch)
+  -> 36 x tree-verify attention -> greedy trace -> padded schedule + host packet
+  -> accepted-suffix compaction of all layers (one launch) -> crop
+  -> position / padding update.
+
+Reported (one JSON line on rank 0):
+  value      KV-commit GB/s: algorithmic bytes of append + compaction (each moved
+             byte read once and written once) / device time of those kernels
+  tree_verify  steps/s = 1 / (mask + 36 attention launches) per step
+  e2e        the same KV-commit metric through the public API with the step's
+             inputs copied from pinned host memory and the packet read back
+  roofline   the append kernel (dominant commit kernel) vs measured HBM copy peak
+  cpu_baseline  the CPU oracle on a bounded sample of the same work
+
+``--impl reference`` times the CPU restatement of the reference's path (the
+reference is Python/torch and cannot run on the GPU host) on the host cores.
+Multi-GPU (torchrun): every rank owns its own batch of sequences (weak scaling)
+and one int64 acceptance-counter all_reduce runs per step on a side stream.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS = ROOT / 'MEASURED_PEAKS.json'
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+METRIC = 'KV-commit GB/s (% HBM peak) + tree-verify steps/s, Qwen2.5-3B geom B=64'
+EOS = 151643
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=20)
+    p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    p.add_argument('--workload', default='qwen25_3b')
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-e2e', action='store_true')
+    return p.parse_args()
+
+
+def peaks():
+    if PEAKS.exists():
+        d = json.loads(PEAKS.read_text())
+        return float(d['hbm_gbs']), float(d['bf16_tflops']), 'measured'
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
+
+
+def workload_config(wl, extra=None):
+    cfg = {'workload': f'{wl.name}: {wl.layers} layers, batch {wl.batch}, {wl.q_heads}q/{wl.kv_heads}kv heads x '
+                       f'{wl.dim}, {wl.dtype}, max_len {wl.capacity}, prefix {wl.prefix}, {wl.nodes}-node tree '
+                       f'depth {wl.depth} top-k {wl.topk}, accepted {wl.accept}',
+           'layers': wl.layers, 'batch_per_gpu': wl.batch, 'tree_rows': wl.rows,
+           'l2': 'inputs larger than L2: each step streams > 4 GB of KV pools'}
+    cfg.update(extra or {})
+    return cfg
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.gpu_id}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(', ') for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for name, flag in zip(names, r[5:9]):
+                    if flag.strip().lower() in ('active', '1'):
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': mx, 'samples': len(sm), 'reasons': sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic verify-round state
+# ---------------------------------------------------------------------------
+class Round:
+    """Device-resident inputs of the stationary verify round (shapes never change)."""
+
+    def __init__(self, wl, device, seed, sample_sets=8):
+        import torch
+        from analysis_spec_b200 import workloads as W
+        from analysis_spec_b200.opd_static_cache import OPDStaticCache
+        from analysis_spec_b200.tree_verification import PackedTree
+        self.wl = wl
+        self.device = device
+        dtype = getattr(torch, wl.dtype)
+        self.dtype = dtype
+        rng = np.random.RandomState(seed)
+        B, R, H, D = wl.batch, wl.rows, wl.kv_heads, wl.dim
+        self.prefix = W.prefix_lengths(rng, wl.prefix, B)
+        self.past = int(self.prefix.max())
+        cols = wl.capacity
+        pad = np.zeros((B, cols), dtype=bool)
+        pad[:, :self.past] = W.left_padding(self.prefix, self.past)
+        self.pad = torch.from_numpy(pad).to(device)
+        self.pad_commit = torch.zeros_like(self.pad)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        scale = wl.qkv_scale
+        self.cache = OPDStaticCache(wl.capacity, batch_capacity=B)
+        prefix_k = (scale * torch.randn(B, H, self.past, D, device=device, generator=gen)).to(dtype)
+        prefix_v = (scale * torch.randn(B, H, self.past, D, device=device, generator=gen)).to(dtype)
+        for l in range(wl.layers):
+            self.cache.update(prefix_k, prefix_v, l)
+        del prefix_k, prefix_v
+        # per-layer projections laid out (B, R, heads * D) and viewed (B, heads, R, D)
+        self.k_proj = [(scale * torch.randn(B, R, H * D, device=device, generator=gen)).to(dtype)
+                       for _ in range(wl.layers)]
+        self.v_proj = [(scale * torch.randn(B, R, H * D, device=device, generator=gen)).to(dtype)
+                       for _ in range(wl.layers)]
+        self.q_proj = [(scale * torch.randn(B, R, wl.q_heads * D, device=device, generator=gen)).to(dtype)
+                       for _ in range(wl.layers)]
+        self.keys = [x.view(B, R, H, D).transpose(1, 2) for x in self.k_proj]
+        self.values = [x.view(B, R, H, D).transpose(1, 2) for x in self.v_proj]
+        self.queries = [x.view(B, R, wl.q_heads, D).transpose(1, 2) for x in self.q_proj]
+        self.out = [torch.empty(B, R, wl.q_heads, D, device=device, dtype=dtype) for _ in range(wl.layers)]
+        parents, tokens = W.packed_trees(rng, B, wl.nodes, wl.depth, wl.topk)
+        self.parents_np, self.tokens_np = parents, tokens
+        self.tree = PackedTree(torch.from_numpy(parents).to(device), torch.from_numpy(tokens).to(device),
+                               torch.zeros(B, R, dtype=torch.long, device=device), wl.depth)
+        self.samples = []
+        for _ in range(sample_sets):
+            acc = W.accepted_lengths(rng, wl.accept, B)
+            self.samples.append(torch.from_numpy(W.samples_for(rng, parents, tokens, acc)).to(device))
+        width = wl.depth + 1
+        self.path_ws = [torch.empty(B, width, dtype=torch.long, device=device) for _ in range(3)] + \
+                       [torch.empty(B, dtype=torch.long, device=device)]
+        self.pad_ws = [torch.empty(B, width, dtype=torch.bool if i == 2 else torch.long, device=device)
+                       for i in range(3)] + [torch.empty(B, 1, dtype=torch.long, device=device)]
+        self.packet = torch.empty(B, width + 4, dtype=torch.long, device=device)
+        self.mask_ws = torch.empty(B * R * (self.past + R), dtype=dtype, device=device)
+        self.positions = torch.empty(B, width, dtype=torch.long, device=device)
+        self.past_positions = torch.from_numpy(self.prefix.astype(np.int64)).to(device)
+        self.owners = torch.arange(B, device=device)
+        self.scale = D ** -0.5
+        self.counters = torch.zeros(5, dtype=torch.long, device=device)
+        es = torch.finfo(dtype).bits // 8
+        self.append_bytes = wl.layers * 2 * 2 * B * H * R * D * es
+        self.row_bytes = D * es
+
+    def compact_bytes(self, width, extension):
+        return self.wl.layers * 2 * 2 * self.wl.batch * self.wl.kv_heads * (width - extension) * self.row_bytes
+
+    def attention_flops(self):
+        rows, hq, d = self.wl.rows, self.wl.q_heads, self.wl.dim
+        return float(sum(4 * hq * rows * (int(p) + rows) * d for p in self.prefix)) * self.wl.layers
+
+
+def verify_round(st, i, marks=None):
+    """One verify round; returns (width, extension, rows). `marks` gets CUDA events between phases."""
+    import torch
+    from analysis_spec_b200 import _ops, tree_kernels
+    from analysis_spec_b200.opd_scheduling import schedule
+    from analysis_spec_b200.tree_verification import trace_verified_path
+
+    def mark(k):
+        if marks is not None:
+            marks[k].record()
+
+    mark(0)
+    mask = st.tree.attention_mask(st.past, st.dtype, st.pad, workspace=st.mask_ws)
+    mark(1)
+    views = st.cache.update_layers(st.keys, st.values)
+    mark(2)
+    for l in range(st.wl.layers):
+        _ops.tree_attention(st.queries[l], views[l][0], views[l][1], mask, st.scale, out=st.out[l])
+    mark(3)
+    path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
+    rows, tokens, chosen, newly, last, width = schedule(path, st.past, EOS, st.pad_ws, st.packet, tree_kernels)
+    mark(4)
+    live = [r for r in rows if r[1] == 0]
+    extension = min(r[2] for r in live) if live else width
+    st.cache.commit_accepted(chosen, st.past, extension)
+    _ops.position_update(newly, st.past, st.positions[:, :width], st.past_positions, pad_rows=st.pad_commit,
+                         owners=st.owners)
+    mark(5)
+    st.cache.crop(st.past)  # stationary workload: the next round verifies at the same length
+    return width, extension, rows
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from analysis_spec_b200 import _lib, _ops
+    from analysis_spec_b200.build import build
+    from analysis_spec_b200.workloads import WORKLOADS
+
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    if rank == 0:
+        build()
+    torch.cuda.set_device(local)
+    device = torch.device('cuda', local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
+    _lib.load()
+    wl = WORKLOADS[args.workload]
+    st = Round(wl, device, seed=1000 + rank)
+    side = torch.cuda.Stream(device)
+    pending = None
+
+    def reduce_counters(rows):
+        nonlocal pending
+        acc = sum(r[0] for r in rows)
+        st.counters.copy_(torch.tensor([acc, len(rows) * wl.nodes, len(rows), sum(r[1] for r in rows), len(rows)],
+                                       device=device), non_blocking=True)
+        if world > 1:
+            if pending is not None:
+                pending.wait()
+            side.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(side):
+                pending = dist.all_reduce(st.counters, async_op=True)
+
+    for i in range(args.warmup):
+        _, _, rows = verify_round(st, i)
+        reduce_counters(rows)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(f'GPU-{torch.cuda.get_device_properties(device).uuid}') if rank == 0 else None
+    if clocks:
+        clocks.start()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _lib.profile.reset()
+    _lib.profile.enabled = True
+    widths = []
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        w, e, rows = verify_round(st, i, ev[i])
+        reduce_counters(rows)
+        widths.append((w, e))
+    end.record()
+    torch.cuda.synchronize()
+    _lib.profile.enabled = False
+    launches = _lib.profile.calls
+    kernel_ms = {name: [s.elapsed_time(e) for s, e in pairs] for name, pairs in _lib.profile.events.items()}
+    if pending is not None:
+        pending.wait()
+    if world > 1:
+        dist.barrier()
+    clock = clocks.stop() if clocks else None
+    total_ms = start.elapsed_time(end)
+    commit_ms = sum(ev[i][1].elapsed_time(ev[i][2]) + ev[i][4].elapsed_time(ev[i][5]) for i in range(args.steps))
+    verify_ms = sum(ev[i][0].elapsed_time(ev[i][1]) + ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
+    attn_ms = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
+    commit_bytes = sum(st.append_bytes + st.compact_bytes(w, e) for w, e in widths)
+    times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    total_ms, commit_ms, verify_ms, attn_ms = times.tolist()
+
+    e2e = None if args.no_e2e else measure_e2e(st, args, world)
+    hbm, tflops, peak_kind = peaks()
+    append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
+    append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
+    attn_launch_ms = float(np.mean(kernel_ms['speckv_tree_attention']))
+    attn_tflops = st.attention_flops() / wl.layers / (attn_launch_ms * 1e-3) / 1e12
+    value = world * commit_bytes / (commit_ms * 1e-3) / 1e9
+    result = {
+        'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}',
+                                       'commit_bytes_per_step': commit_bytes // args.steps}),
+        'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4), 'peak_gbs': hbm,
+                      'ms_per_step': round(commit_ms / args.steps, 4)},
+        'tree_verify': {'steps_per_s': round(world * args.steps / (verify_ms * 1e-3), 3),
+                        'ms_per_step': round(verify_ms / args.steps, 4),
+                        'attention_tflops': round(attn_tflops, 2),
+                        'roofline': {'bound': 'tensor', 'achieved': round(attn_tflops, 2), 'peak': tflops,
+                                     'unit': 'TFLOP/s', 'frac': round(attn_tflops / tflops, 4),
+                                     'traffic': None, 'peak_kind': peak_kind}},
+        'roofline': {'bound': 'hbm', 'kernel': 'speckv_append_rows (all layers)', 'achieved': round(append_gbs, 1),
+                     'peak': hbm, 'unit': 'GB/s', 'frac': round(append_gbs / hbm, 4), 'traffic': None,
+                     'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
+        'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
+        'gpu_launches': launches,
+        'clocks': clock,
+        'e2e': e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result['cpu_baseline'] = cpu_baseline(wl, budget_s=12.0)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def measure_e2e(st, args, world):
+    """KV commit through the public API with inputs from pinned host memory and the packet read back."""
+    import torch
+    from analysis_spec_b200 import _ops, tree_kernels
+    from analysis_spec_b200.opd_scheduling import schedule
+    from analysis_spec_b200.tree_verification import trace_verified_path
+    host_k = [x.cpu().pin_memory() for x in st.k_proj]
+    host_v = [x.cpu().pin_memory() for x in st.v_proj]
+    host_s = [s.cpu().pin_memory() for s in st.samples]
+    dev_s = torch.empty_like(st.samples[0])
+    h2d = sum(x.numel() * x.element_size() for x in host_k + host_v) + host_s[0].numel() * 8
+    d2h = st.packet[:, :st.wl.depth + 4].numel() * 8
+    steps = max(2, min(args.steps, 10))
+
+    def one(i):
+        for dst, src in zip(st.k_proj + st.v_proj, host_k + host_v):
+            dst.copy_(src, non_blocking=True)
+        dev_s.copy_(host_s[i % len(host_s)], non_blocking=True)
+        st.cache.update_layers(st.keys, st.values)
+        path = trace_verified_path(st.tree, dev_s, EOS, workspace=st.path_ws)
+        rows, _, chosen, newly, _, width = schedule(path, st.past, EOS, st.pad_ws, st.packet, tree_kernels)
+        live = [r for r in rows if r[1] == 0]
+        ext = min(r[2] for r in live) if live else width
+        st.cache.commit_accepted(chosen, st.past, ext)
+        _ops.position_update(newly, st.past, st.positions[:, :width], st.past_positions, pad_rows=st.pad_commit,
+                             owners=st.owners)
+        st.cache.crop(st.past)
+        return st.append_bytes + st.compact_bytes(width, ext)
+
+    for i in range(2):
+        one(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    moved = sum(one(i) for i in range(steps))
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=st.device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return {'value': round(world * moved / (ms * 1e-3) / 1e9, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': h2d,
+            'd2h_bytes_per_step': d2h, 'steps': steps}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle's restatement of the reference's KV commit
+# ---------------------------------------------------------------------------
+class CpuCommit:
+    """Bounded sample of the KV commit on host cores: `layers` of the workload's layers, full batch."""
+
+    def __init__(self, wl, layers, seed=7):
+        from analysis_spec_b200 import workloads as W
+        from oracle import oracle
+        self.oracle = oracle
+        oracle.set_threads(os.cpu_count() or 1)
+        rng = np.random.RandomState(seed)
+        self.wl, self.layers = wl, layers
+        B, R, H, D = wl.batch, wl.rows, wl.kv_heads, wl.dim
+        itemsize = 2 if wl.dtype != 'float32' else 4
+        dt = np.uint16 if itemsize == 2 else np.float32
+        self.past = int(W.prefix_lengths(rng, wl.prefix, B).max())
+        cap = self.past + R
+        self.kp = [rng.randint(0, 1 << 15, size=(B, H, cap, D)).astype(dt) for _ in range(layers)]
+        self.vp = [rng.randint(0, 1 << 15, size=(B, H, cap, D)).astype(dt) for _ in range(layers)]
+        self.src = [rng.randint(0, 1 << 15, size=(B, R, H, D)).astype(dt).transpose(0, 2, 1, 3)
+                    for _ in range(2 * layers)]
+        parents, tokens = W.packed_trees(rng, B, wl.nodes, wl.depth, wl.topk)
+        self.parents, self.tokens = parents, tokens
+        self.samples = [W.samples_for(rng, parents, tokens, W.accepted_lengths(rng, wl.accept, B)) for _ in range(4)]
+        self.append_bytes = layers * 2 * 2 * B * H * R * D * itemsize
+        self.row_bytes = D * itemsize
+
+    def step(self, i):
+        o, wl = self.oracle, self.wl
+        for l in range(self.layers):
+            o.append(self.kp[l], self.vp[l], self.src[2 * l], self.src[2 * l + 1], self.past)
+        ctx = np.zeros_like(self.parents)
+        pt, pi, pc, pl = o.trace_path(self.parents, self.tokens, ctx, self.samples[i % 4], EOS, wl.depth + 1)
+        _, idx, _, _, packet, width = o.pad_schedule(pt, pi, pl, self.past, EOS)
+        live = packet[packet[:, 1] == 0]
+        ext = int(live[:, 2].min()) if len(live) else width
+        for l in range(self.layers):
+            o.compact_suffix(self.kp[l], self.vp[l], wl.batch, self.past + wl.rows, idx, self.past, ext)
+        return self.append_bytes + self.layers * 2 * 2 * wl.batch * wl.kv_heads * (width - ext) * self.row_bytes
+
+
+def cpu_baseline(wl, budget_s=12.0, layers=4):
+    cpu = CpuCommit(wl, layers)
+    cpu.step(0)
+    moved, steps, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        moved += cpu.step(steps)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {'value': round(moved / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cpu.oracle.max_threads(), 'kind': 'port',
+            'sample': f'{layers} of {wl.layers} layers per step (full batch {wl.batch}, 61 tree rows), '
+                      f'{steps} steps in {dt:.1f} s: append + trace + schedule + compaction by the C/numpy oracle'}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', 0))
+    if rank != 0:
+        return
+    from analysis_spec_b200.workloads import WORKLOADS
+    wl = WORKLOADS[args.workload]
+    cpu = CpuCommit(wl, layers=4)
+    for i in range(args.warmup):
+        cpu.step(i)
+    moved, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        moved += cpu.step(i)
+    dt = time.perf_counter() - t0
+    value = moved / dt / 1e9
+    sample = (f'each step: 4 of {wl.layers} layers of the workload (full batch {wl.batch}); append + trace + '
+              'schedule + compaction by the C/numpy restatement of the reference (the reference itself is '
+              'Python/torch code that is not present on the GPU host)')
+    print(json.dumps({
+        'impl': 'reference', 'metric': METRIC, 'value': round(value, 4), 'unit': 'GB/s', 'n_gpus': args.gpus,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(dt * 1e3 / args.steps, 3),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+        'config': workload_config(wl, {'parallelism': 'host cores'}),
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cpu.oracle.max_threads(), 'kind': 'port',
+                         'sample': sample},
+        'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }), flush=True)
+
+
+if __name__ == '__main__':
+    a = parse()
+    if a.impl == 'reference':
+        run_reference(a)
+    else:
+        run_ours(a)

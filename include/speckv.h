@@ -1,0 +1,224 @@
+/*
+ * speckv.h - C ABI of the B200 (sm_100a) static-KV-cache / tree-verify library.
+ *
+ * Every entry point takes plain device pointers, element counts / strides and
+ * a cudaStream_t passed as `void*` (NULL = legacy default stream). Nothing here
+ * allocates device memory: buffers (pools, index lists, masks, outputs, the
+ * optional remap scratch) are owned by the caller. Every call is asynchronous
+ * on `stream` and returns a status code; the message for a non-zero status is
+ * available from speckv_last_error() on the calling thread.
+ *
+ * Pool layout (one K pool and one V pool per layer, as the reference keeps):
+ *   pool[batch_capacity][heads][capacity][dim], row = dim * elem_bytes bytes,
+ *   contiguous. A "row" below is one (sequence, head, position) vector.
+ *
+ * Layer-batched calls take host arrays of `layers` device pointers (K pools and
+ * V pools); all layers of one call share geometry. At most SPECKV_MAX_LAYERS
+ * layers per call.
+ *
+ * Index inputs (int64) that address cache rows are bounds-checked on the
+ * device: an out-of-range entry is skipped and recorded in a device-side error
+ * word that speckv_device_error() reads back and clears. Kernels never trap.
+ */
+#ifndef SPECKV_H
+#define SPECKV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPECKV_OK 0
+#define SPECKV_EINVAL 1      /* bad argument (host-side check) */
+#define SPECKV_ECUDA 2       /* a CUDA runtime call failed */
+#define SPECKV_ENOSUPPORT 3  /* shape outside what this build handles */
+
+#define SPECKV_MAX_LAYERS 64
+
+/* Device error word kinds (upper 16 bits of the word; lower 48 = offending value). */
+#define SPECKV_DERR_REMAP_INDEX 1
+#define SPECKV_DERR_COMPACT_INDEX 2
+#define SPECKV_DERR_MOVE_INDEX 3
+#define SPECKV_DERR_TREE_INDEX 4
+#define SPECKV_DERR_OWNER_INDEX 5
+
+/* dtype codes for masks / attention operands */
+#define SPECKV_F32 0
+#define SPECKV_BF16 1
+#define SPECKV_F16 2
+
+/* ---- library state -------------------------------------------------------- */
+
+/* ABI version (major*100 + minor). */
+int speckv_version(void);
+
+/* Message of the last non-zero status returned on this thread. */
+const char* speckv_last_error(void);
+
+/* Copy the device error word of the current device to *word (0 = none) and
+ * clear it. Synchronises `stream`. */
+int speckv_device_error(uint64_t* word, void* stream);
+
+/* ---- KV rows: append / grow --------------------------------------------- */
+
+/* Append `rows` new positions for every (sequence, head) of `layers` layers:
+ *   pool[b][h][length + t][:] = src[b][h][t][:]   for b < batch, h < heads, t < rows
+ * Sources are strided views (B, H, rows, dim) with unit stride on dim and the
+ * given element strides on (b, h, t); K and V sources may differ in stride.
+ * Replaces StaticAppendLayer.update's two copies
+ * (helper/opd_static_cache.py:106-107) and, with length = 0 and the old pool as
+ * source, the history copy of StaticAppendLayer._grow (:88-90). */
+int speckv_append_rows(void* const* key_pools, void* const* value_pools,
+                       const void* const* key_srcs, const void* const* value_srcs,
+                       int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                       int64_t dim, int64_t capacity, int64_t length,
+                       const int64_t* key_src_strides, const int64_t* value_src_strides,
+                       int32_t elem_bytes, void* stream);
+
+/* ---- KV rows: accepted-suffix compaction ------------------------------- */
+
+/* For every layer, K and V, sequence b < batch and head h < heads:
+ *   tmp[j]                 = pool[b][h][chosen[b][extension + j]]   j < width - extension
+ *   pool[b][h][past + extension + j] = tmp[j]
+ * (all reads of one (b, h) happen before its writes, as the reference's
+ * gather-into-scratch then copy). `length` is the visible length the chosen
+ * positions must lie below. Replaces compact_suffix_inplace
+ * (helper/opd_scheduling.py:357-380) and its per-layer loop
+ * (helper/opd_generate.py:637-641) with one launch. */
+int speckv_compact_suffix(void* const* key_pools, void* const* value_pools, int32_t layers,
+                          int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
+                          int64_t length, const int64_t* chosen, int64_t chosen_stride_b,
+                          int64_t chosen_stride_w, int64_t past, int64_t extension,
+                          int64_t width, int32_t elem_bytes, void* stream);
+
+/* ---- KV rows: batch remap (repeat / select) ---------------------------- */
+
+/* Row remap over the live prefix [0, length) of every layer:
+ *   pool'[i][h][t][:] = pool[indices[i]][h][t][:]   i < new_batch
+ * with arbitrary permutations and duplicates (all reads before writes).
+ * indices[i] must lie in [0, batch_capacity). `scratch` (scratch_bytes) is only
+ * used when new_batch rows of one position do not fit on chip; it then needs
+ * 2 * new_batch * heads * length * dim * elem_bytes bytes. Replaces
+ * remap_rows (helper/opd_kv_kernels.py:34-40) called per layer from
+ * StaticAppendLayer.batch_select_indices (helper/opd_static_cache.py:118-149). */
+int speckv_remap_rows(void* const* key_pools, void* const* value_pools, int32_t layers,
+                      const int64_t* indices, int64_t new_batch, int64_t batch_capacity,
+                      int64_t heads, int64_t dim, int64_t capacity, int64_t length,
+                      void* scratch, int64_t scratch_bytes, int32_t elem_bytes, void* stream);
+
+/* Scratch bytes speckv_remap_rows needs for this geometry (0 when the remap
+ * runs in a single on-chip pass). Host-only, no CUDA call. */
+int64_t speckv_remap_scratch_bytes(int64_t new_batch, int64_t heads, int64_t dim, int64_t length,
+                                   int32_t elem_bytes);
+
+/* ---- KV rows: release of finished rows (swap-remove) ------------------- */
+
+/* pool[destinations[j]][h][t][:] = pool[sources[j]][h][t][:] for t < length,
+ * j < count; sources and destinations disjoint. Replaces move_tail_rows
+ * (helper/opd_kv_kernels.py:56-58) called per layer from
+ * StaticAppendLayer.swap_remove (helper/opd_static_cache.py:157-174). */
+int speckv_move_rows(void* const* key_pools, void* const* value_pools, int32_t layers,
+                     const int64_t* sources, const int64_t* destinations, int64_t count,
+                     int64_t batch_capacity, int64_t heads, int64_t dim, int64_t capacity,
+                     int64_t length, int32_t elem_bytes, void* stream);
+
+/* ---- tree kernels (helper/tree_kernels.py plugin) ----------------------- */
+
+/* Re-index the confidence-selected draft nodes into a parent-closed packed
+ * tree with the root at row 0 (helper/tree_verification.py:200-227):
+ *   parents[b][0] = -1, tokens[b][0] = -1, contexts[b][0] = 0,
+ *   parents[b][j+1] = packed row of full_parents[b][chosen[b][j]] (root = 0),
+ *   tokens[b][j+1] = all_tokens[b][chosen[b][j]], contexts[b][j+1] = full_contexts[b][chosen[b][j]].
+ * full_* are contiguous (batch, full_count), chosen contiguous (batch,
+ * packed_count); outputs (batch, packed_count + 1) with row stride
+ * out_stride_b. A node whose parent is not an earlier packed row is recorded
+ * in the device error word (the reference's torch._assert_async). */
+int speckv_pack_tree(const int64_t* full_parents, const int64_t* full_contexts, const int64_t* all_tokens,
+                     const int64_t* chosen, int64_t batch, int64_t full_count, int64_t packed_count,
+                     int64_t* out_parents, int64_t* out_tokens, int64_t* out_contexts,
+                     int64_t out_stride_b, void* stream);
+
+/* Greedy acceptance walk (helper/tree_kernels.py:68-95,
+ * helper/tree_verification.py:286-322). parents/tokens/contexts/samples are
+ * contiguous (batch, rows) int64; outputs (batch, width) with the given
+ * strides; lengths (batch,). */
+int speckv_trace_path(const int64_t* parents, const int64_t* tokens, const int64_t* contexts,
+                      const int64_t* samples, int64_t batch, int64_t rows, int64_t eos,
+                      int64_t* out_tokens, int64_t* out_indices, int64_t* out_contexts,
+                      int64_t out_stride_b, int64_t out_stride_w, int64_t width,
+                      int64_t* lengths, void* stream);
+
+/* Gap-first padded commit layout (helper/tree_verification.py:237-268,
+ * helper/tree_kernels.py:97-137). Inputs (batch, capacity) int64 with strides;
+ * outputs tokens/indices (int64) and mask (bool bytes) (batch, width) with
+ * out strides; last (batch,) with stride last_stride. */
+int speckv_pad_verified_path(const int64_t* tokens, int64_t tok_stride_b, int64_t tok_stride_w,
+                             const int64_t* indices, int64_t idx_stride_b, int64_t idx_stride_w,
+                             const int64_t* lengths, int64_t batch, int64_t capacity,
+                             int64_t width, int64_t past, int64_t eos,
+                             int64_t* out_tokens, int64_t* out_indices, uint8_t* out_mask,
+                             int64_t out_stride_b, int64_t out_stride_w,
+                             int64_t* last, int64_t last_stride, void* stream);
+
+/* Padded schedule + host packet (helper/tree_kernels.py:7-41): as above with
+ * width = max(lengths) computed on the device, plus
+ *   packet[b] = [length, last token == eos, extension, pad ids (capacity)..., snapshot?]
+ * `snapshot` may be NULL (then column capacity + 3 is not written). */
+int speckv_pad_schedule(const int64_t* tokens, int64_t tok_stride_b, int64_t tok_stride_w,
+                        const int64_t* indices, int64_t idx_stride_b, int64_t idx_stride_w,
+                        const int64_t* lengths, int64_t batch, int64_t capacity,
+                        int64_t past, int64_t eos,
+                        int64_t* out_tokens, int64_t* out_indices, uint8_t* out_mask,
+                        int64_t out_stride_b, int64_t out_stride_w,
+                        int64_t* last, int64_t last_stride,
+                        int64_t* packet, int64_t packet_stride_b, int64_t packet_stride_w,
+                        const int64_t* snapshot, void* stream);
+
+/* Additive tree mask (batch, 1, rows, past + rows) (helper/tree_kernels.py:139-155,
+ * helper/tree_verification.py:19-42): 0 where column <= past or column is
+ * past + an ancestor of the row within `steps` parent hops (row itself
+ * included), the dtype's lowest finite value elsewhere. If `pad` is non-NULL,
+ * columns with pad[b * pad_stride_b + c] != 0 are forced to the lowest value
+ * (the masked_fill_ at helper/opd_generate.py:483-484). */
+int speckv_tree_mask(const int64_t* parents, int64_t batch, int64_t rows, int64_t past,
+                     int64_t steps, void* mask, int32_t dtype, const uint8_t* pad,
+                     int64_t pad_stride_b, void* stream);
+
+/* Position / padding update after a commit (helper/opd_generate.py:556-558,
+ * 644-650):
+ *   pad_rows[owners[b]][past + j] = newly_padded[b][j]          (if pad_rows)
+ *   pad_live[b][past + j]         = newly_padded[b][j]          (if pad_live)
+ *   positions[b][j] = past_positions[b] + #{k <= j : !newly_padded[b][k]}
+ *   past_positions[b] = positions[b][width - 1]
+ * newly_padded is (batch, width) bool bytes with row stride np_stride_b. */
+int speckv_position_update(uint8_t* pad_rows, int64_t pad_rows_stride, int64_t pad_rows_count,
+                           const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
+                           const uint8_t* newly_padded, int64_t np_stride_b, int64_t batch,
+                           int64_t past, int64_t width, int64_t* positions,
+                           int64_t positions_stride_b, int64_t* past_positions, void* stream);
+
+/* ---- tree-verify attention -------------------------------------------- */
+
+/* GQA attention of `rows` tree queries over kv_len cached positions with an
+ * additive mask, without materialising repeated K/V:
+ *   out[b][r][hq][:] = softmax_c(q[b][hq][r] . k[b][hq / g][c] * scale + mask[b][0][r][c]) v[b][hq/g][c]
+ * g = q_heads / kv_heads. q/k/v element strides are given as (b, h, t) with unit
+ * stride on dim; mask is (batch, 1, rows, kv_len) contiguous in `mask_dtype`
+ * or NULL; out is contiguous (batch, rows, q_heads, dim) in `dtype`.
+ * Replaces repeat_kv + F.scaled_dot_product_attention in transformers'
+ * sdpa_attention_forward (integrations/sdpa_attention.py:56-104) as called from
+ * Qwen2Attention.forward (models/qwen2/modeling_qwen2.py:206-240). */
+int speckv_tree_attention(const void* q, const int64_t* q_strides,
+                          const void* k, const int64_t* k_strides,
+                          const void* v, const int64_t* v_strides,
+                          const void* mask, int32_t mask_dtype,
+                          void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                          int64_t rows, int64_t kv_len, int64_t dim, float scale,
+                          int32_t dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECKV_H */

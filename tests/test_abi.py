@@ -1,0 +1,59 @@
+"""The C-ABI library loads and exports every entry point include/speckv.h declares.
+
+No compute calls here (this runs without a GPU); only host-only entry points
+(version, scratch sizing, argument validation that fails before any CUDA call)
+are exercised.
+"""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from analysis_spec_b200 import _lib
+from analysis_spec_b200.build import build
+
+HEADER = Path(__file__).resolve().parents[1] / 'include' / 'speckv.h'
+
+
+def declared():
+    text = re.sub(r'/\*.*?\*/', '', HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r'\b(speckv_\w+)\s*\(', text)))
+
+
+@pytest.fixture(scope='module')
+def lib():
+    build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+        if name not in ('speckv_last_error', 'speckv_remap_scratch_bytes'):
+            assert name in _lib.SIGNATURES, f'{name} has no ctypes signature'
+
+
+def test_host_only_entry_points(lib):
+    assert lib.speckv_version() == 100
+    # one position of 64 bf16 rows of 128 dims fits on chip: no scratch
+    assert lib.speckv_remap_scratch_bytes(64, 2, 128, 2048, 2) == 0
+    # 1000 rows of 256 fp32 dims (1 MB per position) need the two-phase scratch
+    assert lib.speckv_remap_scratch_bytes(1000, 2, 256, 10, 4) == 2 * 1000 * 2 * 10 * 256 * 4
+
+
+def test_argument_errors_are_reported_without_a_launch(lib):
+    nul = (ctypes.c_void_p * 1)(None)
+    strides = _lib.i64_array([0, 0, 0])
+    with pytest.raises(_lib.SpecKVError, match='layers=0'):
+        _lib.call('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None)
+    with pytest.raises(_lib.SpecKVError, match='null pool'):
+        _lib.call('speckv_move_rows', nul, nul, 1, None, None, 1, 1, 1, 8, 8, 4, 2, None)
+    with pytest.raises(_lib.SpecKVError, match='invalid committed path width'):
+        _lib.call('speckv_pad_verified_path', None, 0, 0, None, 0, 0, None, 1, 4, 9, 0, 0, None, None, None, 0, 0,
+                  None, 0, None)
+    with pytest.raises(_lib.SpecKVError, match='not a multiple'):
+        _lib.call('speckv_tree_attention', None, strides, None, strides, None, strides, None, 0, None, 1, 3, 2, 1, 1,
+                  8, 1.0, 1, None)
