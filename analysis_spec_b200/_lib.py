@@ -14,7 +14,7 @@ MAX_LAYERS = 64
 F32, BF16, F16 = 0, 1, 2
 
 DEVICE_ERROR_KINDS = {1: 'remap index', 2: 'compact index', 3: 'move index', 4: 'tree parent index',
-                      5: 'padding owner index'}
+                      5: 'padding owner index', 6: 'wait timeout'}
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -37,6 +37,9 @@ SIGNATURES = {
                             _i64, _p, _i64, _i64, _p, _p],
     'speckv_tree_mask': [_p, _i64, _i64, _i64, _i64, _p, _i32, _p, _i64, _p],
     'speckv_position_update': [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p],
+    'speckv_tree_mask_bits': [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p],
+    'speckv_tree_attention_bits': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                   _i64, ctypes.c_float, _i32, _p],
     'speckv_tree_attention': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                               ctypes.c_float, _i32, _p],
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],

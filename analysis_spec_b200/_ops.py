@@ -261,6 +261,55 @@ def tree_attention(query, key, value, mask, scale, out=None):
     return out
 
 
+def visibility_words(cols):
+    """32-bit words per tree row of the visibility bitmap (whole 128-column tiles)."""
+    return 4 * (-(-cols // 128))
+
+
+def tree_mask_bits(parents, past, steps, bits, first_col, pad=None):
+    """Bit-packed tree visibility (batch, rows, words) int32 + first visible column per sequence."""
+    _require_cuda(parents, bits, first_col, pad)
+    batch, rows = parents.shape
+    parents = _contig_long('parents', parents)
+    if bits.dtype != torch.int32 or not bits.is_contiguous() or bits.shape[:2] != (batch, rows):
+        raise ValueError('bits must be a contiguous (batch, rows, words) int32 tensor')
+    if first_col.dtype != torch.int32 or first_col.numel() < batch:
+        raise ValueError('first_col must be an int32 tensor of batch entries')
+    pad_stride = 0
+    if pad is not None:
+        if pad.dtype != torch.bool or pad.stride(-1) != 1 or pad.shape[-1] < past + rows:
+            raise ValueError('pad must be a bool (batch, columns) tensor covering past + rows columns')
+        pad_stride = pad.stride(0)
+    _lib.call('speckv_tree_mask_bits', parents.data_ptr(), batch, rows, int(past), int(steps), _ptr(pad), pad_stride,
+              bits.data_ptr(), bits.shape[2], first_col.data_ptr(), _stream(parents))
+
+
+def _check_qkv(query, key, value):
+    if query.dtype not in _DTYPE_CODE or key.dtype != query.dtype or value.dtype != query.dtype:
+        raise ValueError('query/key/value must share a float dtype')
+    if query.stride(3) != 1 or key.stride(3) != 1 or value.stride(3) != 1:
+        raise ValueError('query/key/value need unit stride on head_dim')
+    if tuple(value.shape) != tuple(key.shape) or key.shape[0] != query.shape[0] or key.shape[3] != query.shape[3]:
+        raise ValueError('key/value shapes do not match the query')
+
+
+def tree_attention_bits(query, key, value, bits, first_col, scale, out=None):
+    """GQA attention with visibility from tree_mask_bits (no dense mask read)."""
+    _require_cuda(query, key, value, bits, first_col)
+    _check_qkv(query, key, value)
+    batch, q_heads, rows, dim = query.shape
+    kv_heads, kv_len = key.shape[1], key.shape[2]
+    if bits.dtype != torch.int32 or not bits.is_contiguous() or bits.shape[:2] != (batch, rows):
+        raise ValueError('bits must be a contiguous (batch, rows, words) int32 tensor')
+    if out is None:
+        out = torch.empty((batch, rows, q_heads, dim), device=query.device, dtype=query.dtype)
+    _lib.call('speckv_tree_attention_bits', query.data_ptr(), _lib.i64_array(query.stride()[:3]), key.data_ptr(),
+              _lib.i64_array(key.stride()[:3]), value.data_ptr(), _lib.i64_array(value.stride()[:3]),
+              bits.data_ptr(), bits.shape[2], _ptr(first_col), out.data_ptr(), batch, q_heads, kv_heads, rows,
+              kv_len, dim, float(scale), _DTYPE_CODE[query.dtype], _stream(query))
+    return out
+
+
 def device_error(device=None):
     """Reads and clears the library's device error word; returns (kind, value) or None."""
     import ctypes

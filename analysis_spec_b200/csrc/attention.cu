@@ -1,9 +1,60 @@
-// C-ABI entry of the tree-verify attention: validates arguments and picks the
-// kernel for the shape.
+// C-ABI entries of the tree-verify attention: validate arguments and pick the
+// kernel for the shape (tcgen05 kernel for head dim 128 in bf16/fp16 with
+// 16-byte aligned rows, the CUDA-core kernel otherwise).
 #include "common.cuh"
 #include "attention.cuh"
 
 using namespace speckv;
+
+namespace {
+
+int check(const char* fn, const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+          const int64_t* vs, const void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rows,
+          int64_t kv_len, int64_t dim) {
+  if (batch < 0 || q_heads < 1 || kv_heads < 1 || rows < 0 || kv_len < 0 || dim < 1)
+    return fail(SPECKV_EINVAL, "%s: bad sizes", fn);
+  if (q_heads % kv_heads != 0)
+    return fail(SPECKV_EINVAL, "%s: %lld query heads not a multiple of %lld kv heads", fn, (long long)q_heads,
+                (long long)kv_heads);
+  if (batch == 0 || rows == 0) return SPECKV_OK;
+  if (kv_len == 0) return fail(SPECKV_EINVAL, "%s: empty key/value sequence", fn);
+  if (!q || !k || !v || !out || !qs || !ks || !vs) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  return SPECKV_OK;
+}
+
+void fill(AttnArgs& a, const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
+          const int64_t* vs, void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rows,
+          int64_t kv_len, int64_t dim, float scale, int32_t dtype) {
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = qs[i];
+    a.ks[i] = ks[i];
+    a.vs[i] = vs[i];
+  }
+  a.batch = batch;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.rows = rows;
+  a.kv_len = kv_len;
+  a.dim = dim;
+  a.scale = scale;
+  a.dtype = dtype;
+  a.mask = nullptr;
+  a.mask_dtype = SPECKV_F32;
+  a.bits = nullptr;
+  a.row_words = 0;
+  a.first_col = nullptr;
+}
+
+int launch(const AttnArgs& a, cudaStream_t s) {
+  if (sm100_supported(a)) return attention_sm100(a, s);
+  return attention_generic(a, s);
+}
+
+}  // namespace
 
 extern "C" int speckv_tree_attention(const void* q, const int64_t* q_strides,
                                      const void* k, const int64_t* k_strides,
@@ -13,20 +64,34 @@ extern "C" int speckv_tree_attention(const void* q, const int64_t* q_strides,
                                      int64_t rows, int64_t kv_len, int64_t dim, float scale,
                                      int32_t dtype, void* stream) {
   const char* fn = "speckv_tree_attention";
-  if (batch < 0 || q_heads < 1 || kv_heads < 1 || rows < 0 || kv_len < 0 || dim < 1)
-    return fail(SPECKV_EINVAL, "%s: bad sizes", fn);
-  if (q_heads % kv_heads != 0)
-    return fail(SPECKV_EINVAL, "%s: %lld query heads not a multiple of %lld kv heads", fn, (long long)q_heads,
-                (long long)kv_heads);
-  if (batch == 0 || rows == 0) return SPECKV_OK;
-  if (kv_len == 0) return fail(SPECKV_EINVAL, "%s: empty key/value sequence", fn);
-  if (!q || !k || !v || !out || !q_strides || !k_strides || !v_strides) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  int st = check(fn, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim);
+  if (st || batch == 0 || rows == 0) return st;
   if (mask != nullptr && mask_dtype != SPECKV_F32 && mask_dtype != SPECKV_BF16 && mask_dtype != SPECKV_F16)
     return fail(SPECKV_EINVAL, "%s: unsupported mask dtype %d", fn, mask_dtype);
   AttnArgs a;
-  a.q = q; a.k = k; a.v = v; a.mask = mask; a.out = out;
-  for (int i = 0; i < 3; ++i) { a.qs[i] = q_strides[i]; a.ks[i] = k_strides[i]; a.vs[i] = v_strides[i]; }
-  a.batch = batch; a.q_heads = q_heads; a.kv_heads = kv_heads; a.rows = rows; a.kv_len = kv_len; a.dim = dim;
-  a.scale = scale; a.dtype = dtype; a.mask_dtype = mask_dtype;
-  return attention_generic(a, static_cast<cudaStream_t>(stream));
+  fill(a, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim, scale, dtype);
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  return launch(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
+                                          const void* k, const int64_t* k_strides,
+                                          const void* v, const int64_t* v_strides,
+                                          const uint32_t* bits, int64_t row_words, const int32_t* first_col,
+                                          void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                          int64_t rows, int64_t kv_len, int64_t dim, float scale,
+                                          int32_t dtype, void* stream) {
+  const char* fn = "speckv_tree_attention_bits";
+  int st = check(fn, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim);
+  if (st || batch == 0 || rows == 0) return st;
+  if (bits == nullptr) return fail(SPECKV_EINVAL, "%s: null visibility bits", fn);
+  if (row_words < 4 * ((kv_len + 127) / 128))
+    return fail(SPECKV_EINVAL, "%s: row_words %lld below 4 * ceil(kv_len / 128)", fn, (long long)row_words);
+  AttnArgs a;
+  fill(a, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim, scale, dtype);
+  a.bits = bits;
+  a.row_words = row_words;
+  a.first_col = first_col;
+  return launch(a, static_cast<cudaStream_t>(stream));
 }

@@ -10,8 +10,11 @@ struct AttnArgs {
   const void* q;
   const void* k;
   const void* v;
-  const void* mask;  // (batch, 1, rows, kv_len) contiguous, or null
-  void* out;         // (batch, rows, q_heads, dim) contiguous
+  const void* mask;         // dense additive (batch, 1, rows, kv_len) contiguous, or null
+  const uint32_t* bits;     // or bit-packed visibility (batch, rows, row_words)
+  long long row_words;
+  const int* first_col;     // optional with bits: first visible column per sequence
+  void* out;                // (batch, rows, q_heads, dim) contiguous
   long long qs[3], ks[3], vs[3];  // element strides (b, h, t); dim stride is 1
   long long batch, q_heads, kv_heads, rows, kv_len, dim;
   float scale;
@@ -20,5 +23,9 @@ struct AttnArgs {
 
 // CUDA-core path (any head dim <= 256, any dtype).
 int attention_generic(const AttnArgs& a, cudaStream_t s);
+
+// tcgen05 / TMEM / TMA path: head dim 128, bf16 or fp16, 16-byte aligned rows.
+bool sm100_supported(const AttnArgs& a);
+int attention_sm100(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace speckv

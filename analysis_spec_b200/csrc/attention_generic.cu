@@ -79,14 +79,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_generic_kernel(AttnArgs a) 
         const float* kr = Kt + lane * (D + 1);
         for (int d = 0; d < D; ++d) acc = fmaf(qr[d], kr[d], acc);
         s = acc * a.scale;
-        if (mask != nullptr) s += to_f<M>(mask[(b * a.rows + r) * a.kv_len + col]);
+        if (a.bits != nullptr) {
+          const uint32_t w = a.bits[(b * a.rows + r) * a.row_words + (col >> 5)];
+          if (!((w >> (col & 31)) & 1u)) s = -INFINITY;
+        } else if (mask != nullptr) {
+          s += to_f<M>(mask[(b * a.rows + r) * a.kv_len + col]);
+        }
       }
       float tmax = s;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
       const float mnew = fmaxf(m[i], tmax);
-      const float p = col < a.kv_len ? expf(s - mnew) : 0.f;
-      const float corr = expf(m[i] - mnew);
+      const float base = mnew == -INFINITY ? 0.f : mnew;  // rows with nothing visible yet stay at 0
+      const float p = col < a.kv_len ? expf(s - base) : 0.f;
+      const float corr = expf(m[i] - base);
       float psum = p;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
@@ -109,7 +115,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_generic_kernel(AttnArgs a) 
   for (int i = 0; i < 4; ++i) {
     const long long r = r0 + warp * 4 + i;
     if (r >= a.rows) continue;
-    const float inv = 1.f / l[i];
+    const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
     T* orow = out + ((b * a.rows + r) * a.q_heads + hq) * a.dim;
 #pragma unroll
     for (int j = 0; j < kMaxD; ++j) {

@@ -240,6 +240,53 @@ __global__ void __launch_bounds__(kMaskThreads) tree_mask_kernel(const int64_t* 
 }
 
 // ---------------------------------------------------------------------------
+// bit-packed visibility: CTA per (row, sequence); thread per 32-column word.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kMaskThreads) tree_bits_kernel(const int64_t* __restrict__ parents, long long rows,
+                                                                 long long past, long long steps,
+                                                                 const uint8_t* __restrict__ pad, long long pad_sb,
+                                                                 uint32_t* bits, long long row_words, int* first_col,
+                                                                 unsigned long long* err) {
+  __shared__ long long anc[kMaxSteps];
+  __shared__ int nanc;
+  const long long r = blockIdx.x;
+  const long long b = blockIdx.y;
+  if (threadIdx.x == 0) {
+    long long cur = r;
+    int n = 0;
+    for (long long k = 0; k < steps && k < kMaxSteps; ++k) {
+      if (cur >= 0) anc[n++] = cur;
+      const long long at = cur > 0 ? cur : 0;
+      if (at >= rows) {
+        record_error(err, SPECKV_DERR_TREE_INDEX, at);
+        break;
+      }
+      cur = parents[b * rows + at];
+    }
+    nanc = n;
+  }
+  __syncthreads();
+  const long long cols = past + rows;
+  uint32_t* out = bits + (b * rows + r) * row_words;
+  for (long long w = threadIdx.x; w < row_words; w += kMaskThreads) {
+    uint32_t word = 0;
+    const long long c0 = w * 32;
+    if (c0 < cols) {
+      for (int i = 0; i < 32; ++i) {
+        const long long c = c0 + i;
+        if (c >= cols) break;
+        bool vis = c <= past;
+        for (int k = 0; k < nanc && !vis; ++k) vis = c == past + anc[k];
+        if (vis && pad != nullptr && pad[b * pad_sb + c]) vis = false;
+        word |= (vis ? 1u : 0u) << i;
+      }
+    }
+    out[w] = word;
+    if (r == 0 && word != 0) atomicMin(first_col + b, (int)(c0 + __ffs(word) - 1));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // position / padding update: one warp per sequence.
 // ---------------------------------------------------------------------------
 __global__ void position_update_kernel(uint8_t* pad_rows, long long prs, long long pad_count, const int64_t* owners,
@@ -388,6 +435,30 @@ extern "C" int speckv_tree_mask(const int64_t* parents, int64_t batch, int64_t r
   dim3 grid((unsigned)rows, (unsigned)batch, (unsigned)chunks);
   tree_mask_kernel<<<grid, kMaskThreads, 0, static_cast<cudaStream_t>(stream)>>>(parents, rows, past, steps, mask,
                                                                                  dtype, pad, pad_stride_b, err);
+  return check_launch(fn);
+}
+
+extern "C" int speckv_tree_mask_bits(const int64_t* parents, int64_t batch, int64_t rows, int64_t past, int64_t steps,
+                                     const uint8_t* pad, int64_t pad_stride_b, uint32_t* bits, int64_t row_words,
+                                     int32_t* first_col, void* stream) {
+  const char* fn = "speckv_tree_mask_bits";
+  if (batch < 0 || rows < 1 || past < 0 || steps < 0) return fail(SPECKV_EINVAL, "%s: bad sizes", fn);
+  if (steps > kMaxSteps) return fail(SPECKV_ENOSUPPORT, "%s: %lld parent hops exceed %d", fn, (long long)steps, kMaxSteps);
+  const long long cols = past + rows;
+  if (row_words < 4 * ((cols + 127) / 128))
+    return fail(SPECKV_EINVAL, "%s: row_words %lld below 4 * ceil(%lld / 128)", fn, (long long)row_words, cols);
+  if (batch == 0) return SPECKV_OK;
+  if (!parents || !bits || !first_col) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  if (batch > 65535) return fail(SPECKV_ENOSUPPORT, "%s: batch above 65535", fn);
+  unsigned long long* err = device_error_word();
+  if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 0x7f7f7f7f: larger than any column, lowered by atomicMin in the kernel
+  cudaError_t e = cudaMemsetAsync(first_col, 0x7f, (size_t)batch * sizeof(int32_t), s);
+  if (e != cudaSuccess) return fail(SPECKV_ECUDA, "%s: %s", fn, cudaGetErrorString(e));
+  dim3 grid((unsigned)rows, (unsigned)batch);
+  tree_bits_kernel<<<grid, kMaskThreads, 0, s>>>(parents, rows, past, steps, pad, pad_stride_b, bits, row_words,
+                                                 first_col, err);
   return check_launch(fn);
 }
 

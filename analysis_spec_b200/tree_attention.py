@@ -22,6 +22,10 @@ def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0
     if dropout:
         raise ValueError('tree_verify_attention is an inference kernel (dropout must be 0)')
     scale = scaling if scaling is not None else query.shape[-1] ** -0.5
+    vis = attention_mask if hasattr(attention_mask, 'first_col') else getattr(attention_mask, '_speckv_visibility',
+                                                                            None)
+    if vis is not None and key.shape[-2] == vis.past + vis.rows and query.shape[2] == vis.rows:
+        return _ops.tree_attention_bits(query, key, value, vis.bits, vis.first_col, scale), None
     mask = attention_mask
     if mask is not None and mask.shape[-1] > key.shape[-2]:
         mask = mask[:, :, :, :key.shape[-2]]

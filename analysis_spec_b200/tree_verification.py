@@ -49,6 +49,39 @@ class PackedTree:
             mask[padding_positions[:, 0], 0, :, padding_positions[:, 1]] = torch.finfo(dtype).min
         return mask
 
+    def visibility(self, past_length, padding=None, *, workspace=None):
+        """Bit-packed form of ``attention_mask`` for the tensor-core attention.
+
+        Built once per verify round and shared by every layer: (batch, rows,
+        words) int32 bits (bit c of a row = column c visible) plus the first
+        visible column of each sequence, so fully padded key tiles are skipped.
+        ``padding`` is a (batch, columns) bool bitmap of hidden columns.
+        """
+        batch, rows = self.parents.shape
+        words = _ops.visibility_words(past_length + rows)
+        if workspace is not None and workspace[0].numel() >= batch * rows * words and workspace[1].numel() >= batch:
+            bits = workspace[0].view(-1)[:batch * rows * words].view(batch, rows, words)
+            first = workspace[1].view(-1)[:batch]
+        else:
+            bits = torch.empty((batch, rows, words), device=self.parents.device, dtype=torch.int32)
+            first = torch.empty((batch,), device=self.parents.device, dtype=torch.int32)
+        _ops.tree_mask_bits(self.parents, past_length, self.max_depth + 1, bits, first, padding)
+        return TreeVisibility(bits, first, int(past_length), rows)
+
+
+@dataclass
+class TreeVisibility:
+    """Per-round visibility of the verify forward (see PackedTree.visibility)."""
+    bits: torch.Tensor       # (batch, rows, words) int32
+    first_col: torch.Tensor  # (batch,) int32
+    past: int
+    rows: int
+
+    def attach(self, mask):
+        """Tags a dense mask so the registered attention reads these bits instead."""
+        mask._speckv_visibility = self
+        return mask
+
 
 def pack_tree(full_parents, full_contexts, chosen, all_tokens, max_depth, *, workspace=None):
     """Keeps the sorted confidence-selected nodes, re-indexed with the root as row 0."""

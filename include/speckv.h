@@ -42,6 +42,7 @@ extern "C" {
 #define SPECKV_DERR_MOVE_INDEX 3
 #define SPECKV_DERR_TREE_INDEX 4
 #define SPECKV_DERR_OWNER_INDEX 5
+#define SPECKV_DERR_TIMEOUT 6  /* a bounded wait inside a kernel expired; value = wait site */
 
 /* dtype codes for masks / attention operands */
 #define SPECKV_F32 0
@@ -216,6 +217,26 @@ int speckv_tree_attention(const void* q, const int64_t* q_strides,
                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
                           int64_t rows, int64_t kv_len, int64_t dim, float scale,
                           int32_t dtype, void* stream);
+
+/* Bit-packed visibility of the tree mask for the tensor-core attention:
+ *   bits[b][r][w] bit i = 1 iff column 32 w + i is visible to tree row r
+ * with the same rule as speckv_tree_mask (columns >= past + rows are 0), and
+ * first_col[b] = the first column any row of sequence b sees (tiles before it
+ * are skipped). row_words must be >= 4 * ceil((past + rows) / 128). */
+int speckv_tree_mask_bits(const int64_t* parents, int64_t batch, int64_t rows, int64_t past, int64_t steps,
+                          const uint8_t* pad, int64_t pad_stride_b, uint32_t* bits, int64_t row_words,
+                          int32_t* first_col, void* stream);
+
+/* speckv_tree_attention with visibility taken from speckv_tree_mask_bits output
+ * instead of a dense mask (masked scores contribute exactly 0). first_col may
+ * be NULL. */
+int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
+                               const void* k, const int64_t* k_strides,
+                               const void* v, const int64_t* v_strides,
+                               const uint32_t* bits, int64_t row_words, const int32_t* first_col,
+                               void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                               int64_t rows, int64_t kv_len, int64_t dim, float scale,
+                               int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -80,6 +80,78 @@ def test_random_trees_vs_oracle(batch, hq, hkv, rows, past, dim):
     check(out, expect)
 
 
+def test_visibility_bits_match_mask_rule():
+    rng = np.random.RandomState(11)
+    for batch, rows, past, depth in ((3, 17, 40, 4), (64, 61, 2048, 6), (2, 130, 7, 20)):
+        parents = np.full((batch, rows), -1, dtype=np.int64)
+        for b in range(batch):
+            for r in range(1, rows):
+                parents[b, r] = rng.randint(max(0, r - 5), r)
+        pad = np.zeros((batch, past + rows), dtype=bool)
+        for b in range(batch):
+            pad[b, :rng.randint(0, past + 1)] = True
+        tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(parents).cuda(),
+                          torch.from_numpy(parents).cuda(), depth)
+        vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+        bits = vis.bits.cpu().numpy().view(np.uint32)
+        unpacked = np.unpackbits(bits.view(np.uint8), bitorder='little').reshape(batch, rows, -1)
+        expect = oracle.tree_visible(parents, past, depth + 1, pad=pad)
+        assert np.array_equal(unpacked[:, :, :past + rows].astype(bool), expect)
+        assert not unpacked[:, :, past + rows:].any()
+        first = expect.any(axis=1).argmax(axis=1)
+        assert np.array_equal(vis.first_col.cpu().numpy(), first)
+
+
+@pytest.mark.parametrize('batch,hq,hkv,rows,past,ragged', [(4, 16, 2, 61, 700, True), (3, 28, 4, 61, 300, True),
+                                                          (2, 40, 8, 61, 260, True), (2, 16, 2, 17, 3000, True),
+                                                          (1, 16, 2, 1, 129, False), (5, 8, 2, 33, 127, False)])
+def test_tensor_core_bits_path_vs_oracle(batch, hq, hkv, rows, past, ragged):
+    q, k, v, mask, parents, pad = random_case(batch, hq, hkv, rows, past, 128, seed=batch * 13 + hq, ragged=ragged)
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(parents).cuda(),
+                      torch.from_numpy(parents).cuda(), rows)
+    vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+    out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    dense = _ops.tree_attention(q, k, v, mask, 128 ** -0.5)
+    expect = oracle.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                              oracle.additive_mask(oracle.tree_visible(parents, past, rows, pad=pad), 'bfloat16'),
+                              128 ** -0.5)
+    check(out, expect)
+    check(dense, expect)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
+def test_tensor_core_full_size_tree_verify_layer():
+    """Qwen2.5-3B tree-verify layer: batch 64, 16q/2kv x 128, 61 tree rows, prefixes U{256..3072}
+    left-padded to one length; checked on a slice of sequences against the float32 oracle."""
+    from analysis_spec_b200 import workloads as W
+    rng = np.random.RandomState(5)
+    batch, hq, hkv, rows, dim = 64, 16, 2, 61, 128
+    prefix = W.prefix_lengths(rng, ('uniform', 256, 3072), batch)
+    past = int(prefix.max())
+    parents, tokens = W.packed_trees(rng, batch, rows - 1, 6, 10)
+    pad = np.zeros((batch, past + rows), dtype=bool)
+    pad[:, :past] = W.left_padding(prefix, past)
+    gen = torch.Generator(device='cuda').manual_seed(5)
+    q = (0.5 * torch.randn(batch, rows, hq * dim, device='cuda', generator=gen)).bfloat16()
+    q = q.view(batch, rows, hq, dim).transpose(1, 2)
+    kpool = (0.5 * torch.randn(batch, hkv, past + rows + 64, dim, device='cuda', generator=gen)).bfloat16()
+    vpool = (0.5 * torch.randn(batch, hkv, past + rows + 64, dim, device='cuda', generator=gen)).bfloat16()
+    k, v = kpool[:, :, :past + rows], vpool[:, :, :past + rows]
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(tokens).cuda(),
+                      torch.zeros(batch, rows, dtype=torch.long, device='cuda'), 6)
+    vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+    out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, dim ** -0.5)
+    visible = oracle.tree_visible(parents, past, 7, pad=pad)
+    for sl in (slice(0, 3), slice(30, 32), slice(61, 64)):
+        expect = oracle.attention(q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy(),
+                                  v[sl].float().cpu().numpy(), oracle.additive_mask(visible[sl], 'bfloat16'),
+                                  dim ** -0.5)
+        check(out[sl], expect)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
 def test_registered_interface_and_no_mask():
     name = register()
     from transformers import AttentionInterface
