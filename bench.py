@@ -6,7 +6,7 @@ batch 64, 16 query / 2 KV heads x 128, bf16, max_len 4096, prefixes U{256..2048}
 left-padded to one shared length, 60-node trees of depth 6 / top-k 10, accepted
 length ~ geometric(mean 3.5) capped at 7):
 
-  tree mask (+ padding)  -> append the 61 tree rows of all 36 layers (one launch)
+  tree visibility bits (+ padding) -> append the 61 tree rows of all 36 layers (one launch)
   -> 36 x tree-verify attention -> greedy trace -> padded schedule + host packet
   -> accepted-suffix compaction of all layers (one launch) -> crop
   -> position / padding update.
@@ -14,7 +14,7 @@ length ~ geometric(mean 3.5) capped at 7):
 Reported (one JSON line on rank 0):
   value      KV-commit GB/s: algorithmic bytes of append + compaction (each moved
              byte read once and written once) / device time of those kernels
-  tree_verify  steps/s = 1 / (mask + 36 attention launches) per step
+  tree_verify  steps/s = 1 / (visibility build + 36 attention launches) per step
   e2e        the same KV-commit metric through the public API with the step's
              inputs copied from pinned host memory and the packet read back
   roofline   the append kernel (dominant commit kernel) vs measured HBM copy peak
@@ -180,7 +180,9 @@ class Round:
         self.pad_ws = [torch.empty(B, width, dtype=torch.bool if i == 2 else torch.long, device=device)
                        for i in range(3)] + [torch.empty(B, 1, dtype=torch.long, device=device)]
         self.packet = torch.empty(B, width + 4, dtype=torch.long, device=device)
-        self.mask_ws = torch.empty(B * R * (self.past + R), dtype=dtype, device=device)
+        words = 4 * (-(-(self.past + R) // 128))
+        self.vis_ws = (torch.empty(B * R * words, dtype=torch.int32, device=device),
+                       torch.empty(B, dtype=torch.int32, device=device))
         self.positions = torch.empty(B, width, dtype=torch.long, device=device)
         self.past_positions = torch.from_numpy(self.prefix.astype(np.int64)).to(device)
         self.owners = torch.arange(B, device=device)
@@ -210,12 +212,13 @@ def verify_round(st, i, marks=None):
             marks[k].record()
 
     mark(0)
-    mask = st.tree.attention_mask(st.past, st.dtype, st.pad, workspace=st.mask_ws)
+    vis = st.tree.visibility(st.past, st.pad, workspace=st.vis_ws)
     mark(1)
     views = st.cache.update_layers(st.keys, st.values)
     mark(2)
     for l in range(st.wl.layers):
-        _ops.tree_attention(st.queries[l], views[l][0], views[l][1], mask, st.scale, out=st.out[l])
+        _ops.tree_attention_bits(st.queries[l], views[l][0], views[l][1], vis.bits, vis.first_col, st.scale,
+                                 out=st.out[l])
     mark(3)
     path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
     rows, tokens, chosen, newly, last, width = schedule(path, st.past, EOS, st.pad_ws, st.packet, tree_kernels)
@@ -309,7 +312,7 @@ def run_ours(args):
     hbm, tflops, peak_kind = peaks()
     append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
     append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
-    attn_launch_ms = float(np.mean(kernel_ms['speckv_tree_attention']))
+    attn_launch_ms = float(np.mean(kernel_ms['speckv_tree_attention_bits']))
     attn_tflops = st.attention_flops() / wl.layers / (attn_launch_ms * 1e-3) / 1e12
     value = world * commit_bytes / (commit_ms * 1e-3) / 1e9
     result = {
