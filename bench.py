@@ -54,7 +54,20 @@ def parse():
     p.add_argument('--workload', default='qwen25_3b')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--layers', type=int, default=None, help='override the layer count (small profiling cases)')
+    p.add_argument('--batch', type=int, default=None, help='override the per-GPU batch (small profiling cases)')
     return p.parse_args()
+
+
+def workload(args):
+    from dataclasses import replace
+    from analysis_spec_b200.workloads import WORKLOADS
+    wl = WORKLOADS[args.workload]
+    if args.layers:
+        wl = replace(wl, layers=args.layers)
+    if args.batch:
+        wl = replace(wl, batch=args.batch)
+    return wl
 
 
 def peaks():
@@ -78,21 +91,21 @@ def workload_config(wl, extra=None):
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+    """nvidia-smi samples (every 200 ms) of this GPU's SM clock and throttle reasons."""
+    FIELDS = ('uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
-    def __init__(self, gpu_id):
-        self.gpu_id = gpu_id
+    def __init__(self, uuid):
+        self.uuid = str(uuid).lower().replace('gpu-', '')
         self.proc = None
         self.file = None
 
     def start(self):
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
-            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.gpu_id}', f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '200'], stdout=self.file,
-                                         stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200'], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
@@ -107,6 +120,11 @@ class Clocks:
         self.file.flush()
         rows = [r.split(', ') for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
         os.unlink(self.file.name)
+        uuids = {r[0].strip().lower().replace('gpu-', '') for r in rows if r}
+        if self.uuid in uuids:
+            rows = [r for r in rows if r[0].strip().lower().replace('gpu-', '') == self.uuid]
+        elif len(uuids) != 1:
+            return None
         sm, mx, reasons = [], 0.0, set()
         names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
         for r in rows:
@@ -251,7 +269,7 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
     _lib.load()
-    wl = WORKLOADS[args.workload]
+    wl = workload(args)
     st = Round(wl, device, seed=1000 + rank)
     side = torch.cuda.Stream(device)
     pending = None
@@ -451,9 +469,8 @@ def run_reference(args):
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
-    from analysis_spec_b200.workloads import WORKLOADS
-    wl = WORKLOADS[args.workload]
-    cpu = CpuCommit(wl, layers=4)
+    wl = workload(args)
+    cpu = CpuCommit(wl, layers=min(4, wl.layers))
     for i in range(args.warmup):
         cpu.step(i)
     moved, t0 = 0, time.perf_counter()
