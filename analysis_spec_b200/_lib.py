@@ -28,6 +28,7 @@ SIGNATURES = {
     'speckv_compact_suffix': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32,
                               _p],
     'speckv_remap_rows': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i32, _p],
+    'speckv_remap_rows_static': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],
     'speckv_move_rows': [_pp, _pp, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],
     'speckv_pack_tree': [_p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p],
     'speckv_trace_path': [_p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p],

@@ -103,6 +103,20 @@ def remap_rows(key_pools, value_pools, indices, length, scratch=None):
                   _stream(indices))
 
 
+def remap_rows_static(key_pools, value_pools, indices, length):
+    """remap_rows without scratch from the caller: uses the library's fixed device array
+    (for callers that cannot allocate; concurrent calls on one device must be serialised)."""
+    _require_cuda(key_pools[0], indices)
+    bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
+    if indices.dtype != torch.long or not indices.is_contiguous():
+        raise ValueError('indices must be a contiguous int64 tensor')
+    es = key_pools[0].element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_remap_rows_static', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, indices.data_ptr(),
+                  indices.numel(), bcap, heads, dim, capacity, length, es, _stream(indices))
+
+
 def move_rows(key_pools, value_pools, sources, destinations, length):
     """pool[destinations[j]] = pool[sources[j]] over [0, length) for every layer."""
     _require_cuda(key_pools[0], sources, destinations)

@@ -113,6 +113,32 @@ int speckv_remap_rows(void* const* key_pools, void* const* value_pools, int32_t 
 int64_t speckv_remap_scratch_bytes(int64_t new_batch, int64_t heads, int64_t dim, int64_t length,
                                    int32_t elem_bytes);
 
+/* speckv_remap_rows for callers that cannot allocate device memory: a host
+ * that has handed all device memory to its own pooling allocator up front (a
+ * raw cudaMalloc would fail there), a latency-critical loop where cudaMalloc /
+ * cudaFree would synchronise the device, or a foreign-language binding with no
+ * access to the owning framework's allocator. It takes no scratch argument and
+ * calls no allocator: the gather-then-scatter runs through a fixed
+ * SPECKV_REMAP_STATIC_SCRATCH_BYTES array compiled into the library, which
+ * every GPU that loads it holds until the process exits.
+ * - Limit: 2 * new_batch * heads * dim * elem_bytes (K and V of one position of
+ *   every output row) must fit in the array, else SPECKV_EINVAL; longer
+ *   prefixes are processed in position chunks.
+ * - The first call on each device looks the array's device address up
+ *   (cudaGetSymbolAddress, with that device current); make that first call
+ *   before any stream capture.
+ * - All calls on a device share the one array and leave their data in it.
+ *   Nothing in it needs to start at zero (every byte read was written by the
+ *   same call), but calls that overlap on the GPU (other streams, other host
+ *   threads) race on it: serialise them.
+ * No counterpart in the reference: its remap always allocates its scratch
+ * (helper/opd_static_cache.py:128-132). */
+#define SPECKV_REMAP_STATIC_SCRATCH_BYTES (64ull << 20)
+int speckv_remap_rows_static(void* const* key_pools, void* const* value_pools, int32_t layers,
+                             const int64_t* indices, int64_t new_batch, int64_t batch_capacity,
+                             int64_t heads, int64_t dim, int64_t capacity, int64_t length,
+                             int32_t elem_bytes, void* stream);
+
 /* ---- KV rows: release of finished rows (swap-remove) ------------------- */
 
 /* pool[destinations[j]][h][t][:] = pool[sources[j]][h][t][:] for t < length,
