@@ -510,6 +510,397 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Two-tile persistent kernel (visibility bits). One CTA per SM walks a
+// longest-first list of work items (sequence b, KV head, pair of 128-row tiles);
+// both row tiles of an item consume every K/V tile it loads.
+//
+//   warp 0      TMA producer: K and V tiles in separate 2-stage rings
+//   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
+//               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
+//               warpgroup works while the tensor pipe serves the other tile
+//   warps 4-7   softmax of row tile 0; warps 8-11 softmax of row tile 1: thread =
+//               row = TMEM lane; P (16-bit) goes back into the first 64 columns of
+//               its S buffer and feeds the P.V MMA straight from TMEM.
+// A tcgen05.commit covers every earlier MMA of the issuing thread, so when a
+// softmax warpgroup sees S_t,i complete, P_t,i-1 . V_i-1 has finished too: O_t
+// may be rescaled and the P region rewritten without further waits.
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 384;
+constexpr int kMaxSortB = 1024;
+constexpr uint32_t Q2_OFF = 0;                    // Q tile t at Q2_OFF + t * kTileBytes
+constexpr uint32_t K2_OFF = 2 * kTileBytes;       // K stage s at K2_OFF + s * kTileBytes
+constexpr uint32_t V2_OFF = 4 * kTileBytes;       // V stage s at V2_OFF + s * kTileBytes
+constexpr uint32_t KEY2_OFF = 6 * kTileBytes;     // int keys[kMaxSortB]
+constexpr uint32_t ORD2_OFF = KEY2_OFF + 4 * kMaxSortB;  // int order[kMaxSortB]
+constexpr uint32_t BAR2_OFF = ORD2_OFF + 4 * kMaxSortB;
+constexpr uint32_t SMEM2_BYTES = BAR2_OFF + 256 + 1024;
+__host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u; }
+__host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
+
+enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_Q_FULL = 8, C_S_FULL = 10, C_P_FULL = 12,
+       C_O_FINAL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18 };
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// (a.x * b.x + c.x, a.y * b.y + c.y) and (a.x + b.x, a.y + b.y) on the packed f32x2 pipe
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long ra, rb, rc, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rc) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long ra, rb, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+
+struct Item {
+  int b, kvh, pair;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const Sm100Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + BAR2_OFF;
+  auto bar = [&](int i) { return bar0 + 8u * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + BAR2_OFF + 8 * C_ABORT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BAR2_OFF + 8 * C_TMEM_SLOT);
+  int* keys = reinterpret_cast<int*>(smem + KEY2_OFF);
+  int* order = reinterpret_cast<int*>(smem + ORD2_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_rows = a.group * a.rows;
+  const int pairs = (total_rows + 2 * BM - 1) / (2 * BM);
+  const int per_b = a.kv_heads * pairs;
+  const int n_items = a.batch * per_b;
+  const int n_tiles_all = (a.kv_len + BN - 1) / BN;
+  const bool sorted = a.batch <= kMaxSortB;
+  auto first_tile = [&](int b) {
+    if (a.first_col == nullptr) return 0;
+    const int fc = a.first_col[b];
+    return fc < 0 ? 0 : min(fc / BN, n_tiles_all - 1);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(C_K_FULL + i), 1);
+      mbar_init(bar(C_K_EMPTY + i), 1);
+      mbar_init(bar(C_V_FULL + i), 1);
+      mbar_init(bar(C_V_EMPTY + i), 1);
+      mbar_init(bar(C_Q_FULL + i), 128);
+      mbar_init(bar(C_S_FULL + i), 1);
+      mbar_init(bar(C_P_FULL + i), 128);
+      mbar_init(bar(C_O_FINAL + i), 1);
+    }
+    mbar_init(bar(C_DRAIN), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // longest sequences first: order[rank] = b, ties by index
+  if (sorted) {
+    for (int b = threadIdx.x; b < a.batch; b += kThreads2) keys[b] = n_tiles_all - first_tile(b);
+    __syncthreads();
+    for (int b = threadIdx.x; b < a.batch; b += kThreads2) {
+      const int k = keys[b];
+      int rank = 0;
+      for (int o = 0; o < a.batch; ++o) rank += (keys[o] > k) || (keys[o] == k && o < b);
+      order[rank] = b;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int G = gridDim.x, c = blockIdx.x;
+  // slot k of this CTA -> global position (snake order over the sorted list)
+  auto item_at = [&](int k, Item& it) -> bool {
+    const int p = k * G + ((k & 1) ? (G - 1 - c) : c);
+    if (p >= n_items) return false;
+    const int rank = p / per_b, rem = p % per_b;
+    it.b = sorted ? order[rank] : rank;
+    it.kvh = rem / pairs;
+    it.pair = rem % pairs;
+    return true;
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+      int cnt = 0, issued_k = 0, issued_v = 0;
+      bool ok = true;
+      Item it;
+      for (int k = 0; ok && item_at(k, it); ++k) {
+        const int t0 = first_tile(it.b);
+        for (int i = t0; i < n_tiles_all; ++i, ++cnt) {
+          const int s = cnt & 1;
+          if (cnt >= 2 && !mbar_wait(bar(C_K_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 21)) { ok = false; break; }
+          const uint32_t kd = sbase + K2_OFF + s * kTileBytes;
+          mbar_expect_tx(bar(C_K_FULL + s), kTileBytes);
+          tma_load_4d(kd, &tmk, bar(C_K_FULL + s), 0, i * BN, it.kvh, it.b);
+          tma_load_4d(kd + kTileHalf, &tmk, bar(C_K_FULL + s), 64, i * BN, it.kvh, it.b);
+          issued_k = cnt + 1;
+          if (cnt >= 2 && !mbar_wait(bar(C_V_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 22)) { ok = false; break; }
+          const uint32_t vd = sbase + V2_OFF + s * kTileBytes;
+          mbar_expect_tx(bar(C_V_FULL + s), kTileBytes);
+          tma_load_4d(vd, &tmv, bar(C_V_FULL + s), 0, i * BN, it.kvh, it.b);
+          tma_load_4d(vd + kTileHalf, &tmv, bar(C_V_FULL + s), 64, i * BN, it.kvh, it.b);
+          issued_v = cnt + 1;
+        }
+      }
+      if (*abort_flag) {  // loads still in flight must land before shared memory is released
+        for (int q = issued_k - 2 < 0 ? 0 : issued_k - 2; q < issued_k; ++q) drain_wait(bar(C_K_FULL + (q & 1)), (q >> 1) & 1);
+        for (int q = issued_v - 2 < 0 ? 0 : issued_v - 2; q < issued_v; ++q) drain_wait(bar(C_V_FULL + (q & 1)), (q >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t ab = TypeCode<T>::value;
+      const uint32_t id_s = idesc_f16(ab, 0), id_pv = idesc_f16(ab, 1);
+      int cnt = 0;            // key tiles consumed (global)
+      int sc[2] = {0, 0};     // S / P completions per row tile
+      int ic[2] = {0, 0};     // items per row tile
+      bool ok = true;
+      Item it;
+      auto issue_s = [&](int t, int stage) {
+        const uint32_t kbase = sbase + K2_OFF + stage * kTileBytes;
+        const uint32_t qbase = sbase + Q2_OFF + t * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad = sw128_desc(qbase + (kk >> 2) * kTileHalf + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(kbase + (kk >> 2) * kTileHalf + (kk & 3) * 32, 16, 1024);
+          tc_mma(tmem + S_COL(t), ad, bd, id_s, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(bar(C_S_FULL + t));
+      };
+      auto issue_pv = [&](int t, int stage, bool first) -> bool {
+        if (!mbar_wait(bar(C_P_FULL + t), sc[t] & 1, abort_flag, a.err, 23)) return false;
+        ++sc[t];
+        tc_fence_after();
+        const uint32_t vbase = sbase + V2_OFF + stage * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t bd = sw128_desc(vbase + kk * 2048, kTileHalf, 1024);
+          tc_mma_ts(tmem + O2_COL(t), tmem + S_COL(t) + kk * 8, bd, id_pv, (!first || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
+      for (int k = 0; ok && item_at(k, it); ++k) {
+        const bool act1 = it.pair * 2 * BM + BM < total_rows;
+        const int n = n_tiles_all - first_tile(it.b);
+        ok = mbar_wait(bar(C_Q_FULL + 0), ic[0] & 1, abort_flag, a.err, 24);
+        if (ok && act1) ok = mbar_wait(bar(C_Q_FULL + 1), ic[1] & 1, abort_flag, a.err, 25);
+        tc_fence_after();
+        int prev_stage = 0;
+        for (int i = 0; ok && i < n; ++i, ++cnt) {
+          const int s = cnt & 1;
+          if (!mbar_wait(bar(C_K_FULL + s), (cnt >> 1) & 1, abort_flag, a.err, 26)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(0, s);
+          if (act1 && i > 0) {
+            if (!issue_pv(1, prev_stage, i == 1)) { ok = false; break; }
+            tc_commit(bar(C_V_EMPTY + prev_stage));
+          }
+          if (act1) issue_s(1, s);
+          tc_commit(bar(C_K_EMPTY + s));
+          if (!mbar_wait(bar(C_V_FULL + s), (cnt >> 1) & 1, abort_flag, a.err, 27)) { ok = false; break; }
+          tc_fence_after();
+          if (!issue_pv(0, s, i == 0)) { ok = false; break; }
+          if (!act1) tc_commit(bar(C_V_EMPTY + s));
+          prev_stage = s;
+        }
+        if (ok && act1) {
+          if (issue_pv(1, prev_stage, n == 1)) tc_commit(bar(C_V_EMPTY + prev_stage));
+          else ok = false;
+        }
+        if (!ok) break;
+        tc_commit(bar(C_O_FINAL + 0));
+        ++ic[0];
+        if (act1) {
+          tc_commit(bar(C_O_FINAL + 1));
+          ++ic[1];
+        }
+      }
+      tc_commit(bar(C_DRAIN));  // every MMA of this thread completes before TMEM is released
+      drain_wait(bar(C_DRAIN), 0);
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax warpgroups ----------------
+    const int t = (warp - 4) >> 2;            // row tile of this warpgroup
+    const int row = threadIdx.x - 128 - t * 128;  // 0..127 == TMEM lane
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_addr + S_COL(t);
+    const uint32_t o_addr = tmem + lane_addr + O2_COL(t);
+    const float scale = a.scale_log2;
+    int sc = 0, ic = 0;
+    bool ok = true;
+    Item it;
+    for (int k = 0; ok && item_at(k, it); ++k) {
+      const bool act1 = it.pair * 2 * BM + BM < total_rows;
+      if (t == 1 && !act1) continue;
+      const int t0 = first_tile(it.b);
+      const int n = n_tiles_all - t0;
+      const int grow = it.pair * 2 * BM + t * BM + row;
+      const bool valid = grow < total_rows;
+      const int r = valid ? grow / a.group : 0;
+      const int hq = it.kvh * a.group + (valid ? grow % a.group : 0);
+      {
+        const T* qrow = static_cast<const T*>(a.q) + (long long)it.b * a.qs0 + (long long)hq * a.qs1 +
+                        (long long)r * a.qs2;
+        uint8_t* qt = smem + Q2_OFF + t * kTileBytes;
+#pragma unroll
+        for (int cc = 0; cc < 16; ++cc) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (valid) v = *reinterpret_cast<const uint4*>(qrow + cc * 8);
+          *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v;
+        }
+        fence_proxy_async();
+        mbar_arrive(bar(C_Q_FULL + t));
+      }
+      const uint32_t* brow = a.bits + ((long long)it.b * a.rows + r) * a.row_words;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int i = 0; i < n; ++i) {
+        ok = mbar_wait(bar(C_S_FULL + t), sc & 1, abort_flag, a.err, 28);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        ++sc;
+        tc_fence_after();
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (valid) w = *reinterpret_cast<const uint4*>(brow + (t0 + i) * 4);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+        const bool dense = __all_sync(0xffffffffu, (w.x & w.y & w.z & w.w) == 0xffffffffu);
+        // pass 1: row max of the visible raw scores
+        float mx = -INFINITY;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float x[32];
+          tmem_ld32(s_addr + cc * 32, x);
+          tmem_wait_ld();
+          if (dense) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((words[cc] >> j) & 1u) ? x[j] : -INFINITY);
+          }
+        }
+        const float mxs = mx * scale;
+        const bool grow_max = mxs > m_run + 8.0f;
+        const float m_new = grow_max ? mxs : m_run;
+        const float corr = (grow_max && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
+        if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            float o[32];
+            tmem_ld32(o_addr + cc * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] *= corr;
+            tmem_st32(o_addr + cc * 32, o);
+          }
+        }
+        m_run = m_new;
+        const float2 sc2 = make_float2(scale, scale);
+        const float2 neg = make_float2(m_run == -INFINITY ? 0.f : -m_run, m_run == -INFINITY ? 0.f : -m_run);
+        float2 sum2 = make_float2(0.f, 0.f);
+        // pass 2: P = 2^(s * scale - m) written over the first 64 columns of S
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float x[32];
+          tmem_ld32(s_addr + cc * 32, x);
+          tmem_wait_ld();
+          if (!dense) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] = ((words[cc] >> j) & 1u) ? x[j] : -INFINITY;
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            float2 e = ffma2(make_float2(x[j], x[j + 1]), sc2, neg);
+            e.x = ex2(e.x);
+            e.y = ex2(e.y);
+            sum2 = fadd2(sum2, e);
+            pk[j >> 1] = pack2<T>(e.x, e.y);
+          }
+          tmem_st16(s_addr + cc * 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(C_P_FULL + t));
+        l_run = l_run * corr + (sum2.x + sum2.y);
+      }
+      if (!ok) break;
+      ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      ++ic;
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T* orow = static_cast<T*>(a.out) + (((long long)it.b * a.rows + r) * a.q_heads + hq) * HD;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float o[32];
+        tmem_ld32(o_addr + cc * 32, o);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 v;
+            v.x = pack2<T>(o[j] * inv, o[j + 1] * inv);
+            v.y = pack2<T>(o[j + 2] * inv, o[j + 3] * inv);
+            v.z = pack2<T>(o[j + 4] * inv, o[j + 5] * inv);
+            v.w = pack2<T>(o[j + 6] * inv, o[j + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + cc * 32 + j) = v;
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -547,6 +938,24 @@ int launch_sm100(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& 
   const long long grid = (long long)s.batch * s.kv_heads * s.mtiles;
   kern<<<(unsigned)grid, kThreads, SMEM_BYTES, stream>>>(mk, mv, s);
   return check_launch("speckv_tree_attention(sm100)");
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
+template <typename T>
+int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, cudaStream_t stream) {
+  auto kern = attn_pair_kernel<T>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+  const long long pairs = ((long long)s.group * s.rows + 2 * BM - 1) / (2 * BM);
+  const long long items = (long long)s.batch * s.kv_heads * pairs;
+  const long long grid = items < sm_count() ? items : sm_count();
+  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, s);
+  return check_launch("speckv_tree_attention_bits(sm100)");
 }
 
 }  // namespace
@@ -592,8 +1001,7 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   s.err = err;
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
-    return bf ? launch_sm100<__nv_bfloat16, 0, float>(mk, mv, s, stream)
-              : launch_sm100<__half, 0, float>(mk, mv, s, stream);
+    return bf ? launch_pair<__nv_bfloat16>(mk, mv, s, stream) : launch_pair<__half>(mk, mv, s, stream);
   }
   switch (a.mask == nullptr ? SPECKV_F32 : a.mask_dtype) {
     case SPECKV_BF16:

@@ -91,7 +91,7 @@ def workload_config(wl, extra=None):
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
-    """nvidia-smi samples (every 200 ms) of this GPU's SM clock and throttle reasons."""
+    """nvidia-smi samples (every 20 ms) of this GPU's SM clock and throttle reasons."""
     FIELDS = ('uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
@@ -105,7 +105,7 @@ class Clocks:
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200'], stdout=self.file, stderr=subprocess.DEVNULL)
+                                          '-lms', '20'], stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
