@@ -97,6 +97,17 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -381,12 +392,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Q row -> swizzled shared tile (zeros for padding rows)
     {
       const T* qrow = static_cast<const T*>(a.q) + (long long)b * a.qs0 + (long long)hq * a.qs1 + (long long)r * a.qs2;
+      uint4 v[16];  // all loads in flight before the first shared-memory store
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        *reinterpret_cast<uint4*>(smem + Q_OFF + sw_chunk(t, c)) = v;
-      }
+      for (int c = 0; c < 16; ++c) v[c] = valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(smem + Q_OFF + sw_chunk(t, c)) = v[c];
       fence_proxy_async();
       mbar_arrive(bar(B_Q_READY));
     }
@@ -518,14 +528,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
 //               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
 //               warpgroup works while the tensor pipe serves the other tile
-//   warps 4-7   softmax of row tile 0; warps 8-11 softmax of row tile 1: thread =
-//               row = TMEM lane; P (16-bit) goes back into the first 64 columns of
+//   warps 2-5   softmax of row tile 0; warps 6-9 softmax of row tile 1: thread =
+//               row = TMEM lane (warp % 4 picks the lane quarter); S is read once
+//               into registers, P (16-bit) goes back into the first 64 columns of
 //               its S buffer and feeds the P.V MMA straight from TMEM.
 // A tcgen05.commit covers every earlier MMA of the issuing thread, so when a
 // softmax warpgroup sees S_t,i complete, P_t,i-1 . V_i-1 has finished too: O_t
 // may be rescaled and the P region rewritten without further waits.
 // ---------------------------------------------------------------------------
-constexpr int kThreads2 = 384;
+constexpr int kThreads2 = 320;
 constexpr int kMaxSortB = 1024;
 constexpr uint32_t Q2_OFF = 0;                    // Q tile t at Q2_OFF + t * kTileBytes
 constexpr uint32_t K2_OFF = 2 * kTileBytes;       // K stage s at K2_OFF + s * kTileBytes
@@ -537,8 +548,8 @@ constexpr uint32_t SMEM2_BYTES = BAR2_OFF + 256 + 1024;
 __host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u; }
 __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
 
-enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_Q_FULL = 8, C_S_FULL = 10, C_P_FULL = 12,
-       C_O_FINAL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18 };
+enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
+       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18 };
 
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
@@ -547,6 +558,12 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
@@ -577,6 +594,36 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   float2 d;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
   return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 8 on the FMA pipe (relieves the MUFU ex2 unit, which
+// alone would need ~1 us per key tile for the two softmax warpgroups).
+// Range reduction 2^x = 2^n * 2^f, n = round(x) via the 1.5 * 2^23 addition,
+// f = x - n in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients are a
+// minimax fit of the relative error on [-0.5, 0.5] (linear program over 4001
+// points; max relative error 7.5e-5 in fp32 Horner form); 2^n is added to the
+// exponent field as an integer. Inputs at or below -126 (masked scores are
+// -inf) give exactly +0; the reduction runs on x clamped to -126 so the exponent
+// sum never leaves the float range.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
+  const float2 t = fadd2(xc, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = fadd2(xc, make_float2(-n.x, -n.y));
+  float2 p = ffma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111251f, 0.2426111251f));
+  p = ffma2(p, f, make_float2(0.6932609678f, 0.6932609678f));
+  p = ffma2(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  // (bits(t) << 23) keeps exactly n << 23: the 0x4B400000 of the rounding constant shifts out
+  const float rx = __uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23));
+  const float ry = __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23));
+  return make_float2(x.x > -126.f ? rx : 0.f, x.y > -126.f ? ry : 0.f);
 }
 
 struct Item {
@@ -616,10 +663,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mbar_init(bar(C_K_EMPTY + i), 1);
       mbar_init(bar(C_V_FULL + i), 1);
       mbar_init(bar(C_V_EMPTY + i), 1);
-      mbar_init(bar(C_Q_FULL + i), 128);
       mbar_init(bar(C_S_FULL + i), 1);
-      mbar_init(bar(C_P_FULL + i), 128);
       mbar_init(bar(C_O_FINAL + i), 1);
+      mbar_init(bar(C_Q_FULL + i), 128);
+      mbar_init(bar(C_P_FULL + i), 128);
     }
     mbar_init(bar(C_DRAIN), 1);
     *abort_flag = 0;
@@ -699,14 +746,22 @@ __global__ void __launch_bounds__(kThreads2, 1)
       int ic[2] = {0, 0};     // items per row tile
       bool ok = true;
       Item it;
+      // Descriptor bases, computed once; a K step only adds a constant to the
+      // start-address field (16-byte units): K-major +32 B per 16 elements inside a
+      // 128-byte swizzle atom and +16 KB per 64-element half, V (MN-major) +2 KB.
+      const uint64_t q_desc[2] = {sw128_desc(sbase + Q2_OFF, 16, 1024),
+                                  sw128_desc(sbase + Q2_OFF + kTileBytes, 16, 1024)};
+      const uint64_t k_desc[2] = {sw128_desc(sbase + K2_OFF, 16, 1024),
+                                  sw128_desc(sbase + K2_OFF + kTileBytes, 16, 1024)};
+      const uint64_t v_desc[2] = {sw128_desc(sbase + V2_OFF, kTileHalf, 1024),
+                                  sw128_desc(sbase + V2_OFF + kTileBytes, kTileHalf, 1024)};
       auto issue_s = [&](int t, int stage) {
-        const uint32_t kbase = sbase + K2_OFF + stage * kTileBytes;
-        const uint32_t qbase = sbase + Q2_OFF + t * kTileBytes;
+        const uint64_t ad = q_desc[t], bd = k_desc[stage];
+        const uint32_t d = tmem + S_COL(t);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t ad = sw128_desc(qbase + (kk >> 2) * kTileHalf + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(kbase + (kk >> 2) * kTileHalf + (kk & 3) * 32, 16, 1024);
-          tc_mma(tmem + S_COL(t), ad, bd, id_s, kk > 0 ? 1u : 0u);
+          const uint64_t step = (uint64_t)((kk >> 2) * (kTileHalf >> 4) + (kk & 3) * 2);
+          tc_mma(d, ad + step, bd + step, id_s, kk > 0 ? 1u : 0u);
         }
         tc_commit(bar(C_S_FULL + t));
       };
@@ -714,12 +769,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
         if (!mbar_wait(bar(C_P_FULL + t), sc[t] & 1, abort_flag, a.err, 23)) return false;
         ++sc[t];
         tc_fence_after();
-        const uint32_t vbase = sbase + V2_OFF + stage * kTileBytes;
+        const uint64_t bd = v_desc[stage];
+        const uint32_t d = tmem + O2_COL(t), pa = tmem + S_COL(t);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = sw128_desc(vbase + kk * 2048, kTileHalf, 1024);
-          tc_mma_ts(tmem + O2_COL(t), tmem + S_COL(t) + kk * 8, bd, id_pv, (!first || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma_ts(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, (!first || kk > 0) ? 1u : 0u);
         return true;
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
@@ -761,70 +815,113 @@ __global__ void __launch_bounds__(kThreads2, 1)
       tc_commit(bar(C_DRAIN));  // every MMA of this thread completes before TMEM is released
       drain_wait(bar(C_DRAIN), 0);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 2) {
     // ---------------- softmax warpgroups ----------------
-    const int t = (warp - 4) >> 2;            // row tile of this warpgroup
-    const int row = threadIdx.x - 128 - t * 128;  // 0..127 == TMEM lane
-    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+    const int t = (warp - 2) >> 2;                 // row tile of this warpgroup
+    const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;           // row within the tile == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_addr + S_COL(t);
     const uint32_t o_addr = tmem + lane_addr + O2_COL(t);
     const float scale = a.scale_log2;
-    int sc = 0, ic = 0;
+    struct RowMap {
+      bool valid;
+      int r, hq;
+    };
+    auto row_map = [&](const Item& x) {
+      RowMap m;
+      const int grow = x.pair * 2 * BM + t * BM + row;
+      m.valid = grow < total_rows;
+      m.r = m.valid ? grow / a.group : 0;
+      m.hq = x.kvh * a.group + (m.valid ? grow % a.group : 0);
+      return m;
+    };
+    // Q rows of item x -> swizzled shared tile t (zeros for padding rows), then Q_FULL
+    auto write_q = [&](const Item& x) {
+      const RowMap m = row_map(x);
+      const T* qrow = static_cast<const T*>(a.q) + (long long)x.b * a.qs0 + (long long)m.hq * a.qs1 +
+                      (long long)m.r * a.qs2;
+      uint8_t* qt = smem + Q2_OFF + t * kTileBytes;
+      uint4 v[16];  // all loads in flight before the first shared-memory store
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc)
+        v[cc] = m.valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + cc) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v[cc];
+      fence_proxy_async();
+      mbar_arrive(bar(C_Q_FULL + t));
+    };
+    auto next_item = [&](int& kk, Item& nx) -> bool {
+      for (;; ++kk) {
+        if (!item_at(kk, nx)) return false;
+        if (t == 0 || nx.pair * 2 * BM + BM < total_rows) return true;
+      }
+    };
+    int sc = 0, ic = 0, k = 0;
     bool ok = true;
     Item it;
-    for (int k = 0; ok && item_at(k, it); ++k) {
-      const bool act1 = it.pair * 2 * BM + BM < total_rows;
-      if (t == 1 && !act1) continue;
+    bool have = next_item(k, it);
+    if (have) write_q(it);
+    while (have) {
       const int t0 = first_tile(it.b);
       const int n = n_tiles_all - t0;
-      const int grow = it.pair * 2 * BM + t * BM + row;
-      const bool valid = grow < total_rows;
-      const int r = valid ? grow / a.group : 0;
-      const int hq = it.kvh * a.group + (valid ? grow % a.group : 0);
-      {
-        const T* qrow = static_cast<const T*>(a.q) + (long long)it.b * a.qs0 + (long long)hq * a.qs1 +
-                        (long long)r * a.qs2;
-        uint8_t* qt = smem + Q2_OFF + t * kTileBytes;
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc) {
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (valid) v = *reinterpret_cast<const uint4*>(qrow + cc * 8);
-          *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v;
-        }
-        fence_proxy_async();
-        mbar_arrive(bar(C_Q_FULL + t));
-      }
-      const uint32_t* brow = a.bits + ((long long)it.b * a.rows + r) * a.row_words;
+      const RowMap m = row_map(it);
+      const uint32_t* brow = a.bits + ((long long)it.b * a.rows + m.r) * a.row_words + t0 * 4;
       float m_run = -INFINITY, l_run = 0.f;
       for (int i = 0; i < n; ++i) {
+        const uint4 w = m.valid ? *reinterpret_cast<const uint4*>(brow + i * 4) : make_uint4(0, 0, 0, 0);
         ok = mbar_wait(bar(C_S_FULL + t), sc & 1, abort_flag, a.err, 28);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         ++sc;
         tc_fence_after();
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (valid) w = *reinterpret_cast<const uint4*>(brow + (t0 + i) * 4);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+        float x[BN];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) tmem_ld32(s_addr + cc * 32, x + cc * 32);
+        tmem_wait_ld();
         const bool dense = __all_sync(0xffffffffu, (w.x & w.y & w.z & w.w) == 0xffffffffu);
-        // pass 1: row max of the visible raw scores
-        float mx = -INFINITY;
+        if (!dense) {
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float x[32];
-          tmem_ld32(s_addr + cc * 32, x);
-          tmem_wait_ld();
-          if (dense) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, x[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, ((words[cc] >> j) & 1u) ? x[j] : -INFINITY);
-          }
+          for (int j = 0; j < BN; ++j) x[j] = ((words[j >> 5] >> (j & 31)) & 1u) ? x[j] : -INFINITY;
         }
-        const float mxs = mx * scale;
+        float mx0 = fmax3(x[0], x[1], x[2]), mx1 = fmax3(x[3], x[4], x[5]);
+#pragma unroll
+        for (int j = 6; j + 3 < BN; j += 4) {  // columns 6 .. 125
+          mx0 = fmax3(mx0, x[j], x[j + 1]);
+          mx1 = fmax3(mx1, x[j + 2], x[j + 3]);
+        }
+        const float mxs = fmax3(mx0, mx1, fmaxf(x[BN - 2], x[BN - 1])) * scale;
         const bool grow_max = mxs > m_run + 8.0f;
         const float m_new = grow_max ? mxs : m_run;
         const float corr = (grow_max && m_run != -INFINITY) ? ex2(m_run - m_new) : 1.f;
+        m_run = m_new;
+        const float2 sc2 = make_float2(scale, scale);
+        const float nm = m_run == -INFINITY ? 0.f : -m_run;
+        const float2 neg = make_float2(nm, nm);
+        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};  // independent partial sums: no 64-long add chain
+        // P = 2^(s * scale - m), packed to 16 bits over the first 64 columns of S;
+        // half of the pairs on the MUFU ex2 unit, half by polynomial on the FMA pipe
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            float2 e = __ffma2_rn(make_float2(x[cc * 16 + j], x[cc * 16 + j + 1]), sc2, neg);
+            if ((j >> 1) & 1) {
+              e = exp2_poly2(e);
+            } else {
+              e.x = ex2(e.x);
+              e.y = ex2(e.y);
+            }
+            sum2[(j >> 1) & 3] = __fadd2_rn(sum2[(j >> 1) & 3], e);
+            pk[j >> 1] = pack2<T>(e.x, e.y);
+          }
+          tmem_st8(s_addr + cc * 8, pk);
+        }
         if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+          // O_t holds tiles < i: their P.V MMAs were issued before S_t,i, and the commit
+          // that signalled S_t,i covers them; P_t,i . V_i waits for P_FULL below.
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
             float o[32];
@@ -835,61 +932,47 @@ __global__ void __launch_bounds__(kThreads2, 1)
             tmem_st32(o_addr + cc * 32, o);
           }
         }
-        m_run = m_new;
-        const float2 sc2 = make_float2(scale, scale);
-        const float2 neg = make_float2(m_run == -INFINITY ? 0.f : -m_run, m_run == -INFINITY ? 0.f : -m_run);
-        float2 sum2 = make_float2(0.f, 0.f);
-        // pass 2: P = 2^(s * scale - m) written over the first 64 columns of S
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float x[32];
-          tmem_ld32(s_addr + cc * 32, x);
-          tmem_wait_ld();
-          if (!dense) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) x[j] = ((words[cc] >> j) & 1u) ? x[j] : -INFINITY;
-          }
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float2 e = ffma2(make_float2(x[j], x[j + 1]), sc2, neg);
-            e.x = ex2(e.x);
-            e.y = ex2(e.y);
-            sum2 = fadd2(sum2, e);
-            pk[j >> 1] = pack2<T>(e.x, e.y);
-          }
-          tmem_st16(s_addr + cc * 16, pk);
-        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(C_P_FULL + t));
-        l_run = l_run * corr + (sum2.x + sum2.y);
+        const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+        l_run = l_run * corr + ((s01.x + s01.y) + (s23.x + s23.y));
       }
       if (!ok) break;
+      // The last S_t of this item has completed, so Q tile t is free: stage the next
+      // item now so its first S MMA can overlap this item's epilogue.
+      Item nx;
+      int kn = k + 1;
+      const bool have_next = next_item(kn, nx);
+      if (have_next) write_q(nx);
       ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       ++ic;
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T* orow = static_cast<T*>(a.out) + (((long long)it.b * a.rows + r) * a.q_heads + hq) * HD;
+      T* orow = static_cast<T*>(a.out) + (((long long)it.b * a.rows + m.r) * a.q_heads + m.hq) * HD;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float o[32];
-        tmem_ld32(o_addr + cc * 32, o);
+      for (int cc = 0; cc < 2; ++cc) {
+        float o[64];
+        tmem_ld32(o_addr + cc * 64, o);
+        tmem_ld32(o_addr + cc * 64 + 32, o + 32);
         tmem_wait_ld();
-        if (valid) {
+        if (m.valid) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
+          for (int j = 0; j < 64; j += 8) {
             uint4 v;
             v.x = pack2<T>(o[j] * inv, o[j + 1] * inv);
             v.y = pack2<T>(o[j + 2] * inv, o[j + 3] * inv);
             v.z = pack2<T>(o[j + 4] * inv, o[j + 5] * inv);
             v.w = pack2<T>(o[j + 6] * inv, o[j + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + cc * 32 + j) = v;
+            *reinterpret_cast<uint4*>(orow + cc * 64 + j) = v;
           }
         }
       }
       tc_fence_before();
+      it = nx;
+      k = kn;
+      have = have_next;
     }
   }
   tc_fence_before();
