@@ -254,9 +254,9 @@ def verify_round(st, i, marks=None):
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from analysis_spec_b200 import _lib, _ops
+    from analysis_spec_b200 import _lib
     from analysis_spec_b200.build import build
-    from analysis_spec_b200.workloads import WORKLOADS
+    from analysis_spec_b200.counters import AcceptanceCounters, round_increments
 
     rank = int(os.environ.get('RANK', 0))
     world = int(os.environ.get('WORLD_SIZE', 1))
@@ -271,20 +271,10 @@ def run_ours(args):
     _lib.load()
     wl = workload(args)
     st = Round(wl, device, seed=1000 + rank)
-    side = torch.cuda.Stream(device)
-    pending = None
+    counters = AcceptanceCounters(device)
 
     def reduce_counters(rows):
-        nonlocal pending
-        acc = sum(r[0] for r in rows)
-        st.counters.copy_(torch.tensor([acc, len(rows) * wl.nodes, len(rows), sum(r[1] for r in rows), len(rows)],
-                                       device=device), non_blocking=True)
-        if world > 1:
-            if pending is not None:
-                pending.wait()
-            side.wait_stream(torch.cuda.current_stream(device))
-            with torch.cuda.stream(side):
-                pending = dist.all_reduce(st.counters, async_op=True)
+        counters.add_round(round_increments(rows, wl.nodes))
 
     for i in range(args.warmup):
         _, _, rows = verify_round(st, i)
@@ -311,8 +301,7 @@ def run_ours(args):
     _lib.profile.enabled = False
     launches = _lib.profile.calls
     kernel_ms = {name: [s.elapsed_time(e) for s, e in pairs] for name, pairs in _lib.profile.events.items()}
-    if pending is not None:
-        pending.wait()
+    totals = counters.finish()
     if world > 1:
         dist.barrier()
     clock = clocks.stop() if clocks else None
@@ -322,9 +311,12 @@ def run_ours(args):
     attn_ms = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     commit_bytes = sum(st.append_bytes + st.compact_bytes(w, e) for w, e in widths)
     times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms], device=device, dtype=torch.float64)
+    moved = torch.tensor([float(commit_bytes)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.all_reduce(moved)
     total_ms, commit_ms, verify_ms, attn_ms = times.tolist()
+    job_commit_bytes = moved.item()
 
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
     hbm, tflops, peak_kind = peaks()
@@ -332,7 +324,7 @@ def run_ours(args):
     append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
     attn_launch_ms = float(np.mean(kernel_ms['speckv_tree_attention_bits']))
     attn_tflops = st.attention_flops() / wl.layers / (attn_launch_ms * 1e-3) / 1e12
-    value = world * commit_bytes / (commit_ms * 1e-3) / 1e9
+    value = job_commit_bytes / (commit_ms * 1e-3) / 1e9
     result = {
         'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
@@ -352,6 +344,7 @@ def run_ours(args):
                      'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
         'gpu_launches': launches,
+        'acceptance': totals,
         'clocks': clock,
         'e2e': e2e,
     }
