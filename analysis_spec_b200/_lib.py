@@ -14,7 +14,7 @@ MAX_LAYERS = 64
 F32, BF16, F16 = 0, 1, 2
 
 DEVICE_ERROR_KINDS = {1: 'remap index', 2: 'compact index', 3: 'move index', 4: 'tree parent index',
-                      5: 'padding owner index', 6: 'wait timeout'}
+                      5: 'padding owner index', 6: 'wait timeout', 7: 'scheduling packet'}
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -27,6 +27,8 @@ SIGNATURES = {
     'speckv_append_rows': [_pp, _pp, _pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _i32, _p],
     'speckv_compact_suffix': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32,
                               _p],
+    'speckv_commit_round': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64,
+                            _p, _i64, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _p],
     'speckv_remap_rows': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i32, _p],
     'speckv_remap_rows_static': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],
     'speckv_move_rows': [_pp, _pp, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],

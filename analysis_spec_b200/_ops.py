@@ -82,6 +82,59 @@ def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extensio
                   es, _stream(chosen))
 
 
+def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, newly_padded=None, positions=None,
+                 past_positions=None, pad_rows=None, owners=None, pad_live=None):
+    """Compaction of every layer + position/padding update of one verify round in one launch,
+    with width and extension taken from the device packet (no host round trip).
+
+    `chosen` / `newly_padded` / `positions` are full-width (batch, max_width) schedule outputs.
+    Pass no pools to update positions only, no `positions` to compact only.
+    """
+    key_pools = list(key_pools or [])
+    _require_cuda(packet, chosen, newly_padded, positions, past_positions, pad_rows, owners, pad_live,
+                  *(key_pools[:1]))
+    if packet.dtype != torch.long or packet.dim() != 2 or packet.stride(1) != 1 or packet.shape[1] < 3 or \
+            packet.shape[0] < batch:
+        raise ValueError('packet must be a (batch, >= 3) int64 tensor with unit column stride')
+    widths = []
+    if key_pools:
+        if chosen is None or chosen.dtype != torch.long or chosen.dim() != 2 or chosen.shape[0] < batch:
+            raise ValueError('chosen indices must be a (batch, width) int64 tensor')
+        widths.append(chosen.shape[1])
+    if positions is not None:
+        if newly_padded is None or past_positions is None:
+            raise ValueError('the position update needs newly_padded and past_positions')
+        if newly_padded.stride(1) != 1 or positions.stride(1) != 1 or positions.dtype != torch.long or \
+                past_positions.dtype != torch.long or not past_positions.is_contiguous():
+            raise ValueError('newly_padded / positions need unit column stride; positions must be int64')
+        if newly_padded.shape[0] < batch or positions.shape[0] < batch or past_positions.shape[0] < batch:
+            raise ValueError('position operands do not cover the batch')
+        widths.append(min(newly_padded.shape[1], positions.shape[1]))
+        if owners is not None:
+            owners = _contig_long('owners', owners)
+    if not widths:
+        return
+    max_width = min(widths)
+    pos_args = (_ptr(pad_rows), 0 if pad_rows is None else pad_rows.stride(0),
+                0 if pad_rows is None else pad_rows.shape[0], _ptr(owners), _ptr(pad_live),
+                0 if pad_live is None else pad_live.stride(0), _ptr(newly_padded),
+                0 if newly_padded is None else newly_padded.stride(0), _ptr(positions),
+                0 if positions is None else positions.stride(0), _ptr(past_positions))
+    no_pos = (None, 0, 0, None, None, 0, None, 0, None, 0, None)
+    stream = _stream(packet)
+    if not key_pools:
+        _lib.call('speckv_commit_round', None, None, 0, batch, 1, 1, 1, 0, 1, None, 0, 0, past, packet.data_ptr(),
+                  packet.stride(0), max_width, *pos_args, stream)
+        return
+    _, heads, capacity, dim = _pool_geometry(key_pools[0])
+    es = key_pools[0].element_size()
+    for a, b in _chunks(len(key_pools)):
+        _lib.call('speckv_commit_round', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim, capacity,
+                  length, es, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, packet.data_ptr(),
+                  packet.stride(0), max_width, *(pos_args if a == 0 else no_pos), stream)
+
+
 def remap_scratch_elements(new_batch, heads, dim, length, element_size):
     """Elements of pool dtype the remap needs as scratch (0 for the single on-chip pass)."""
     nbytes = _lib.load().speckv_remap_scratch_bytes(new_batch, heads, dim, length, element_size)

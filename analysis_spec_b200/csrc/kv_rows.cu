@@ -6,8 +6,11 @@
 //
 // These replace the reference's per-layer torch copy_/gather calls and Triton
 // kernels (helper/opd_static_cache.py:99-174, helper/opd_kv_kernels.py:11-58,
-// helper/opd_scheduling.py:357-380); results are byte-identical.
+// helper/opd_scheduling.py:35-58); results are byte-identical.
 #include "common.cuh"
+#include "positions.cuh"
+
+#include <limits.h>
 
 namespace speckv {
 namespace {
@@ -309,6 +312,99 @@ __global__ void __launch_bounds__(kThreads) move_rows_kernel(PoolTable pools, co
 }
 
 // ---------------------------------------------------------------------------
+// commit round: the accepted-suffix compaction of every layer and the
+// per-sequence position / padding update in one launch, with the round's width
+// (longest accepted path) and extension (shortest untouched prefix over live
+// sequences) reduced from the scheduling packet on the device. Nothing waits
+// for the host to read the packet, so the commit runs straight after the
+// packet is written.
+// ---------------------------------------------------------------------------
+struct RoundGeom {
+  CompactGeom c;             // extension and n unused: both come from the packet
+  const int64_t* chosen;     // (batch, >= max_width) cache positions of the padded paths
+  const int64_t* packet;     // (batch, ps) rows [length, eos?, extension, ...]
+  long long ps;
+  uint32_t batch, max_width;
+  uint32_t compact_blocks;   // blocks [0, compact_blocks) compact, the rest update positions
+  PositionArgs pos;          // positions == null: no position update
+};
+
+template <int V, int MAXR>
+__global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools, RoundGeom g,
+                                                                unsigned long long* err) {
+  typedef typename Vec<V>::T T;
+  __shared__ int s_width, s_ext;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    long long wmax = 0, emin = LLONG_MAX;
+    for (uint32_t b = lane; b < g.batch; b += 32) {
+      const int64_t* row = g.packet + (long long)b * g.ps;
+      const long long len = row[0];
+      wmax = len > wmax ? len : wmax;
+      if (row[1] == 0 && row[2] < emin) emin = row[2];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const long long w2 = __shfl_xor_sync(0xffffffffu, wmax, o);
+      const long long e2 = __shfl_xor_sync(0xffffffffu, emin, o);
+      wmax = w2 > wmax ? w2 : wmax;
+      emin = e2 < emin ? e2 : emin;
+    }
+    if (emin == LLONG_MAX) emin = wmax;  // no live sequence: nothing to move
+    const bool ok = wmax <= g.max_width && wmax <= g.c.length - g.c.past && emin >= 0 && emin <= wmax;
+    if (lane == 0) {
+      if (!ok && blockIdx.x == 0) record_error(err, SPECKV_DERR_PACKET, wmax);
+      s_width = ok ? (int)wmax : -1;
+      s_ext = (int)emin;
+    }
+  }
+  __syncthreads();
+  const int width = s_width, ext = s_ext;
+  if (width < 0) return;
+  if (blockIdx.x >= g.compact_blocks) {
+    const long long b = (long long)(blockIdx.x - g.compact_blocks) * (kThreads / 32) + warp;
+    if (b < g.batch && width > 0) position_row(g.pos, b, g.c.past, width, lane, err);
+    return;
+  }
+  const uint32_t group = blockIdx.x * (kThreads / 32) + warp;
+  if (group >= g.c.groups) return;
+  uint32_t tensor, bh, b, h;
+  g.c.bh.divmod(group, tensor, bh);
+  g.c.heads.divmod(bh, b, h);
+  char* base = pools.ptr[tensor] + (long long)b * g.c.sb + (long long)h * g.c.sh;
+  const uint32_t nv = (uint32_t)(width - ext) * g.c.nvec.d;
+  T buf[MAXR];
+  int src[MAXR];  // source position, -1 = skipped (length < 2^31 is checked on the host)
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    const uint32_t i = lane + r * 32;
+    src[r] = -1;
+    if (i < nv) {
+      uint32_t j, lv;
+      g.c.nvec.divmod(i, j, lv);
+      const long long pos = g.chosen[(long long)b * g.c.csb + (long long)(ext + j) * g.c.csw];
+      if (pos < 0 || pos >= g.c.length) {
+        record_error(err, SPECKV_DERR_COMPACT_INDEX, pos);
+      } else {
+        src[r] = (int)pos;
+        buf[r] = load_vec<V>(base + pos * g.c.row_bytes + (long long)lv * V);
+      }
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    const uint32_t i = lane + r * 32;
+    if (i < nv && src[r] >= 0) {
+      uint32_t j, lv;
+      g.c.nvec.divmod(i, j, lv);
+      store_vec<V>(base + (g.c.past + ext + j) * g.c.row_bytes + (long long)lv * V, buf[r]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host helpers
 // ---------------------------------------------------------------------------
 int check_common(const char* fn, void* const* kp, void* const* vp, int32_t layers, int64_t heads,
@@ -466,6 +562,87 @@ extern "C" int speckv_compact_suffix(void* const* key_pools, void* const* value_
         cudaFuncSetAttribute(compact_smem_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       compact_smem_kernel<V><<<(unsigned)groups, kThreads, (size_t)smem, s>>>(pools, chosen, g, err);
     });
+  }
+  return check_launch(fn);
+}
+
+extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_t layers,
+                                   int64_t batch, int64_t heads, int64_t dim, int64_t capacity, int64_t length,
+                                   int32_t elem_bytes, const int64_t* chosen, int64_t chosen_stride_b,
+                                   int64_t chosen_stride_w, int64_t past, const int64_t* packet,
+                                   int64_t packet_stride, int64_t max_width, uint8_t* pad_rows,
+                                   int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
+                                   uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
+                                   int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
+                                   int64_t* past_positions, void* stream) {
+  const char* fn = "speckv_commit_round";
+  if (layers != 0) {
+    int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
+    if (st) return st;
+  }
+  if (batch < 0 || past < 0 || max_width < 1 || length < 0) return fail(SPECKV_EINVAL, "%s: bad sizes", fn);
+  if (layers != 0 && (past > length || length > capacity))
+    return fail(SPECKV_EINVAL, "%s: past %lld / length %lld / capacity %lld inconsistent", fn, (long long)past,
+                (long long)length, (long long)capacity);
+  if (batch == 0 || (layers == 0 && positions == nullptr)) return SPECKV_OK;
+  if (packet == nullptr || packet_stride < 3) return fail(SPECKV_EINVAL, "%s: packet rows need 3 columns", fn);
+  if (layers != 0 && chosen == nullptr) return fail(SPECKV_EINVAL, "%s: null chosen", fn);
+  if (positions != nullptr) {
+    if (!newly_padded || !past_positions) return fail(SPECKV_EINVAL, "%s: null position operand", fn);
+    if (pad_rows != nullptr && (owners == nullptr || past + max_width > pad_rows_stride))
+      return fail(SPECKV_EINVAL, "%s: padding rows need owners and past + width <= row stride", fn);
+    if (pad_live != nullptr && past + max_width > pad_live_stride)
+      return fail(SPECKV_EINVAL, "%s: past + width exceeds live padding row stride", fn);
+  }
+  constexpr int MAXR = 16;
+  const long long row_bytes = layers != 0 ? dim * elem_bytes : 16;
+  const int vec = layers != 0 ? pool_vec(key_pools, value_pools, layers, row_bytes) : 16;
+  const long long nvec = row_bytes / vec;
+  if (!fits_u31(length)) return fail(SPECKV_ENOSUPPORT, "%s: length exceeds 2^31", fn);
+  if (layers != 0 && max_width * nvec > 32 * MAXR)
+    return fail(SPECKV_ENOSUPPORT, "%s: %lld rows of %lld vectors exceed the register stage", fn,
+                (long long)max_width, nvec);
+  const long long groups = 2ll * layers * batch * (layers != 0 ? heads : 0);
+  const long long compact_blocks = (groups + kThreads / 32 - 1) / (kThreads / 32);
+  const long long position_blocks = positions != nullptr ? (batch + kThreads / 32 - 1) / (kThreads / 32) : 0;
+  if (!fits_u31(groups) || !fits_u31(compact_blocks + position_blocks) || !fits_u31(batch * (layers != 0 ? heads : 1)))
+    return fail(SPECKV_ENOSUPPORT, "%s: problem too large for 32-bit indexing", fn);
+  unsigned long long* err = device_error_word();
+  if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
+  PoolTable pools;
+  if (layers != 0) fill_pools(pools, key_pools, value_pools, layers);
+  RoundGeom g;
+  g.c.bh = FastDiv((uint32_t)(batch * (layers != 0 ? heads : 1)));
+  g.c.heads = FastDiv((uint32_t)(layers != 0 ? heads : 1));
+  g.c.nvec = FastDiv((uint32_t)nvec);
+  g.c.row_bytes = row_bytes;
+  g.c.sh = layers != 0 ? capacity * row_bytes : 0;
+  g.c.sb = layers != 0 ? heads * g.c.sh : 0;
+  g.c.length = layers != 0 ? length : past + max_width;
+  g.c.past = past;
+  g.c.extension = 0;
+  g.c.csb = chosen_stride_b;
+  g.c.csw = chosen_stride_w;
+  g.c.n = 0;
+  g.c.groups = (uint32_t)groups;
+  g.chosen = chosen;
+  g.packet = packet;
+  g.ps = packet_stride;
+  g.batch = (uint32_t)batch;
+  g.max_width = (uint32_t)max_width;
+  g.compact_blocks = (uint32_t)compact_blocks;
+  g.pos = PositionArgs{pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
+                       newly_padded, np_stride_b, positions, positions_stride_b, past_positions};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = (unsigned)(compact_blocks + position_blocks);
+  // register stage sized to the widest round the schedule allows (fewer registers, more resident warps)
+  const long long stage = max_width * nvec;
+  if (stage <= 32 * 4) {
+    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 4><<<grid, kThreads, 0, s>>>(pools, g, err));
+  } else if (stage <= 32 * 8) {
+    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 8><<<grid, kThreads, 0, s>>>(pools, g, err));
+  } else {
+    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, MAXR><<<grid, kThreads, 0, s>>>(pools, g, err));
   }
   return check_launch(fn);
 }

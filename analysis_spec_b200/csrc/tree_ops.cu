@@ -5,6 +5,7 @@
 // Semantics follow helper/tree_kernels.py:7-41, 68-155 and
 // helper/tree_verification.py:19-42, 237-322 of the reference.
 #include "common.cuh"
+#include "positions.cuh"
 
 #include <limits.h>
 
@@ -289,41 +290,11 @@ __global__ void __launch_bounds__(kMaskThreads) tree_bits_kernel(const int64_t* 
 // ---------------------------------------------------------------------------
 // position / padding update: one warp per sequence.
 // ---------------------------------------------------------------------------
-__global__ void position_update_kernel(uint8_t* pad_rows, long long prs, long long pad_count, const int64_t* owners,
-                                       uint8_t* pad_live, long long pls, const uint8_t* __restrict__ np,
-                                       long long npsb, long long batch, long long past, long long width,
-                                       int64_t* positions, long long psb, int64_t* past_positions,
+__global__ void position_update_kernel(PositionArgs a, long long batch, long long past, long long width,
                                        unsigned long long* err) {
   const long long b = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
   if (b >= batch) return;
-  long long owner = -1;
-  if (pad_rows != nullptr) {
-    owner = owners[b];
-    if (owner < 0 || owner >= pad_count) {
-      if (lane == 0) record_error(err, SPECKV_DERR_OWNER_INDEX, owner);
-      owner = -1;
-    }
-  }
-  long long carry = past_positions[b];
-  for (long long j0 = 0; j0 < width; j0 += 32) {
-    const long long j = j0 + lane;
-    const bool in = j < width;
-    const uint8_t padded = in ? np[b * npsb + j] : 1;
-    if (in) {
-      if (owner >= 0) pad_rows[owner * prs + past + j] = padded;
-      if (pad_live != nullptr) pad_live[b * pls + past + j] = padded;
-    }
-    int inc = (in && !padded) ? 1 : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += y;
-    }
-    if (in) positions[b * psb + j] = carry + inc;
-    carry += __shfl_sync(0xffffffffu, inc, 31);
-  }
-  if (lane == 0) past_positions[b] = carry;
+  position_row(a, b, past, width, threadIdx.x & 31, err);
 }
 
 }  // namespace
@@ -479,8 +450,9 @@ extern "C" int speckv_position_update(uint8_t* pad_rows, int64_t pad_rows_stride
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   const int threads = 128;
   const long long blocks = (batch * 32 + threads - 1) / threads;
-  position_update_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride, newly_padded, np_stride_b,
-      batch, past, width, positions, positions_stride_b, past_positions, err);
+  const PositionArgs a{pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
+                       newly_padded, np_stride_b, positions, positions_stride_b, past_positions};
+  position_update_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(a, batch, past, width,
+                                                                                            err);
   return check_launch(fn);
 }

@@ -19,6 +19,32 @@ def schedule(path, past, eos, workspace, packet, kernels=None, opd=None):
     Returns (rows, tokens, indices, mask, last, width) with rows the host packet
     [length, eos?, extension, pad ids...] per sequence.
     """
+    return _schedule(path, past, eos, workspace, packet, kernels, opd, None)
+
+
+def schedule_commit(path, past, eos, workspace, packet, cache, positions, past_positions, pad_rows=None,
+                    owners=None, pad_live=None, kernels=None, opd=None):
+    """``schedule`` with the round's commit enqueued on the device before the packet read-back.
+
+    Right after the padded schedule is written, one launch compacts the accepted
+    suffix of every layer of ``cache`` and updates positions / padding, taking
+    width and extension from the device packet (``speckv_commit_round``); the GPU
+    runs the commit while the host waits for the packet. The cache is then
+    cropped to ``past + width``. Same result as ``schedule`` followed by
+    ``cache.commit_accepted(indices, past, extension)`` and
+    ``_ops.position_update(mask, past, positions[:, :width], past_positions, ...)``
+    (helper/opd_generate.py:632-650); returns ``schedule``'s tuple.
+    """
+    def commit(tokens, indices, mask, out_packet):
+        cache.commit_scheduled(indices, past, out_packet, newly_padded=mask, positions=positions,
+                               past_positions=past_positions, pad_rows=pad_rows, owners=owners, pad_live=pad_live)
+
+    result = _schedule(path, past, eos, workspace, packet, kernels, opd, commit)
+    cache.crop(past + result[5])
+    return result
+
+
+def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
     b, capacity = path.tokens.shape
     plugin = kernels if kernels is not None else _default_kernels
     if kernels is not None and opd is not None:
@@ -41,6 +67,8 @@ def schedule(path, past, eos, workspace, packet, kernels=None, opd=None):
         snapshot = (opd.dispatch_snapshot if getattr(opd, 'async_updates', False)
                     else getattr(opd, 'dispatch_count', opd.active_count))
     plugin.pad_schedule(path, past, eos, tokens, indices, mask, last, out_packet, snapshot=snapshot)
+    if commit is not None:
+        commit(tokens, indices, mask, out_packet)
     if reflex:
         rows = packet[:b, :capacity + 4].cpu().tolist()
         opd.host_active_count = rows[0][-1]

@@ -227,6 +227,30 @@ def _repeat_indices(batch, repeats, device):
     return torch.arange(batch, device=device).repeat_interleave(repeats)
 
 
+class LayerViews:
+    """Sequence of per-layer (keys, values) views as of its creation, each built on
+    first access: slicing 2 x layers views up front costs more host time than the
+    one append launch that precedes them."""
+
+    __slots__ = ('_items',)
+
+    def __init__(self, layers):
+        self._items = [(l.key_pool, l.value_pool, l.batch_size, l.length) for l in layers]
+
+    def __len__(self):
+        return len(self._items)
+
+    def __getitem__(self, index):
+        if isinstance(index, slice):
+            return [self[i] for i in range(*index.indices(len(self._items)))]
+        k, v, b, n = self._items[index]
+        return k[:b, :, :n, :], v[:b, :, :n, :]
+
+    def __iter__(self):
+        for i in range(len(self._items)):
+            yield self[i]
+
+
 def _uniform(layers):
     """True when every layer's pools share shape and dtype (one launch can cover them)."""
     first = layers[0]
@@ -381,7 +405,7 @@ class OPDStaticCache(Cache):
                 _ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length)
         for layer, (_, _, end) in zip(layers, prepared):
             layer.length = end
-        return [(l.keys, l.values) for l in layers]
+        return LayerViews(layers)
 
     def commit_accepted(self, chosen, past, extension):
         """Accepted-path commit of every layer in one launch, then crop.
@@ -401,6 +425,29 @@ class OPDStaticCache(Cache):
                     _ops.compact_suffix([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length,
                                         chosen, past, extension, width)
         self.crop(past + width)
+
+    def commit_scheduled(self, chosen, past, packet, newly_padded=None, positions=None, past_positions=None,
+                         pad_rows=None, owners=None, pad_live=None):
+        """``commit_accepted`` with width and extension read from the device packet.
+
+        ``chosen`` (and the position operands) are the full-width schedule
+        outputs; the launch needs no host value of the round, so it can be
+        enqueued before the packet is read back. The caller crops the cache to
+        ``past + width`` once it knows the width.
+        """
+        layers = [l for l in self.layers if l.key_pool is not None]
+        pos = dict(newly_padded=newly_padded, positions=positions, past_positions=past_positions,
+                   pad_rows=pad_rows, owners=owners, pad_live=pad_live)
+        if not layers:
+            _ops.commit_round([], [], packet.shape[0], 0, chosen, past, packet, **pos)
+        elif _uniform(layers):
+            first = layers[0]
+            _ops.commit_round([l.key_pool for l in layers], [l.value_pool for l in layers], first.batch_size,
+                              first.length, chosen, past, packet, **pos)
+        else:
+            for i, layer in enumerate(layers):
+                _ops.commit_round([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length, chosen,
+                                  past, packet, **(pos if i == 0 else {}))
 
     def statistics(self):
         totals = {name: sum(layer.stats[name] for layer in self.layers) for name in LAYER_COUNTERS}

@@ -219,10 +219,10 @@ class Round:
 
 
 def verify_round(st, i, marks=None):
-    """One verify round; returns (width, extension, rows). `marks` gets CUDA events between phases."""
-    import torch
+    """One verify round; returns (width, extension, rows). `marks` gets CUDA events between phases:
+    0 visibility 1 append 2 attention 3 trace + schedule + device commit + packet read-back 4."""
     from analysis_spec_b200 import _ops, tree_kernels
-    from analysis_spec_b200.opd_scheduling import schedule
+    from analysis_spec_b200.opd_scheduling import schedule_commit
     from analysis_spec_b200.tree_verification import trace_verified_path
 
     def mark(k):
@@ -239,14 +239,12 @@ def verify_round(st, i, marks=None):
                                  out=st.out[l])
     mark(3)
     path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
-    rows, tokens, chosen, newly, last, width = schedule(path, st.past, EOS, st.pad_ws, st.packet, tree_kernels)
+    rows, _, _, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
+                                              st.past_positions, pad_rows=st.pad_commit, owners=st.owners,
+                                              kernels=tree_kernels)
     mark(4)
     live = [r for r in rows if r[1] == 0]
     extension = min(r[2] for r in live) if live else width
-    st.cache.commit_accepted(chosen, st.past, extension)
-    _ops.position_update(newly, st.past, st.positions[:, :width], st.past_positions, pad_rows=st.pad_commit,
-                         owners=st.owners)
-    mark(5)
     st.cache.crop(st.past)  # stationary workload: the next round verifies at the same length
     return width, extension, rows
 
@@ -285,7 +283,7 @@ def run_ours(args):
     clocks = Clocks(f'GPU-{torch.cuda.get_device_properties(device).uuid}') if rank == 0 else None
     if clocks:
         clocks.start()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     _lib.profile.reset()
     _lib.profile.enabled = True
@@ -306,16 +304,19 @@ def run_ours(args):
         dist.barrier()
     clock = clocks.stop() if clocks else None
     total_ms = start.elapsed_time(end)
-    commit_ms = sum(ev[i][1].elapsed_time(ev[i][2]) + ev[i][4].elapsed_time(ev[i][5]) for i in range(args.steps))
+    # KV commit = the append launch + the device-scheduled commit launch of every step, each timed by
+    # CUDA events recorded around the launch on the launching stream
+    commit_ms = sum(kernel_ms['speckv_append_rows']) + sum(kernel_ms['speckv_commit_round'])
+    region_ms = sum(ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps))
     verify_ms = sum(ev[i][0].elapsed_time(ev[i][1]) + ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     attn_ms = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     commit_bytes = sum(st.append_bytes + st.compact_bytes(w, e) for w, e in widths)
-    times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms], device=device, dtype=torch.float64)
+    times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms, region_ms], device=device, dtype=torch.float64)
     moved = torch.tensor([float(commit_bytes)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(moved)
-    total_ms, commit_ms, verify_ms, attn_ms = times.tolist()
+    total_ms, commit_ms, verify_ms, attn_ms, region_ms = times.tolist()
     job_commit_bytes = moved.item()
 
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
@@ -332,7 +333,9 @@ def run_ours(args):
         'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}',
                                        'commit_bytes_per_step': commit_bytes // args.steps}),
         'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4), 'peak_gbs': hbm,
-                      'ms_per_step': round(commit_ms / args.steps, 4)},
+                      'ms_per_step': round(commit_ms / args.steps, 4),
+                      'launches': ['speckv_append_rows', 'speckv_commit_round'],
+                      'append_region_ms_per_step': round(region_ms / args.steps, 4)},
         'tree_verify': {'steps_per_s': round(world * args.steps / (verify_ms * 1e-3), 3),
                         'ms_per_step': round(verify_ms / args.steps, 4),
                         'attention_tflops': round(attn_tflops, 2),
@@ -359,8 +362,8 @@ def run_ours(args):
 def measure_e2e(st, args, world):
     """KV commit through the public API with inputs from pinned host memory and the packet read back."""
     import torch
-    from analysis_spec_b200 import _ops, tree_kernels
-    from analysis_spec_b200.opd_scheduling import schedule
+    from analysis_spec_b200 import tree_kernels
+    from analysis_spec_b200.opd_scheduling import schedule_commit
     from analysis_spec_b200.tree_verification import trace_verified_path
     host_k = [x.cpu().pin_memory() for x in st.k_proj]
     host_v = [x.cpu().pin_memory() for x in st.v_proj]
@@ -376,12 +379,11 @@ def measure_e2e(st, args, world):
         dev_s.copy_(host_s[i % len(host_s)], non_blocking=True)
         st.cache.update_layers(st.keys, st.values)
         path = trace_verified_path(st.tree, dev_s, EOS, workspace=st.path_ws)
-        rows, _, chosen, newly, _, width = schedule(path, st.past, EOS, st.pad_ws, st.packet, tree_kernels)
+        rows, _, _, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
+                                                  st.past_positions, pad_rows=st.pad_commit, owners=st.owners,
+                                                  kernels=tree_kernels)
         live = [r for r in rows if r[1] == 0]
         ext = min(r[2] for r in live) if live else width
-        st.cache.commit_accepted(chosen, st.past, ext)
-        _ops.position_update(newly, st.past, st.positions[:, :width], st.past_positions, pad_rows=st.pad_commit,
-                             owners=st.owners)
         st.cache.crop(st.past)
         return st.append_bytes + st.compact_bytes(width, ext)
 
@@ -398,8 +400,10 @@ def measure_e2e(st, args, world):
         import torch.distributed as dist
         t = torch.tensor([ms], device=st.device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    return {'value': round(world * moved / (ms * 1e-3) / 1e9, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': h2d,
+        m = torch.tensor([float(moved)], device=st.device, dtype=torch.float64)
+        dist.all_reduce(m)
+        ms, moved = t.item(), m.item()
+    return {'value': round(moved / (ms * 1e-3) / 1e9, 3), 'unit': 'GB/s', 'h2d_bytes_per_step': h2d,
             'd2h_bytes_per_step': d2h, 'steps': steps}
 
 

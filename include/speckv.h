@@ -43,6 +43,7 @@ extern "C" {
 #define SPECKV_DERR_TREE_INDEX 4
 #define SPECKV_DERR_OWNER_INDEX 5
 #define SPECKV_DERR_TIMEOUT 6  /* a bounded wait inside a kernel expired; value = wait site */
+#define SPECKV_DERR_PACKET 7   /* scheduling packet inconsistent with the commit; value = its width */
 
 /* dtype codes for masks / attention operands */
 #define SPECKV_F32 0
@@ -85,13 +86,39 @@ int speckv_append_rows(void* const* key_pools, void* const* value_pools,
  * (all reads of one (b, h) happen before its writes, as the reference's
  * gather-into-scratch then copy). `length` is the visible length the chosen
  * positions must lie below. Replaces compact_suffix_inplace
- * (helper/opd_scheduling.py:357-380) and its per-layer loop
+ * (helper/opd_scheduling.py:35-58) and its per-layer loop
  * (helper/opd_generate.py:637-641) with one launch. */
 int speckv_compact_suffix(void* const* key_pools, void* const* value_pools, int32_t layers,
                           int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
                           int64_t length, const int64_t* chosen, int64_t chosen_stride_b,
                           int64_t chosen_stride_w, int64_t past, int64_t extension,
                           int64_t width, int32_t elem_bytes, void* stream);
+
+/* ---- KV rows: device-scheduled commit of a verify round ----------------- */
+
+/* speckv_compact_suffix of every layer followed by speckv_position_update, in
+ * one launch, with width and extension read from the scheduling packet on the
+ * device instead of passed by the host:
+ *   width     = max_b packet[b][0]                      (longest accepted path)
+ *   extension = min over b with packet[b][1] == 0 of packet[b][2]
+ *               (= width when every sequence finished)
+ * so the commit can be enqueued right after speckv_pad_schedule, before the
+ * host reads the packet back. `chosen` / `newly_padded` / `positions` are the
+ * full (batch, max_width) padded-schedule outputs; columns >= width are not
+ * read. layers == 0 skips the compaction, positions == NULL skips the position
+ * update. A packet whose width exceeds max_width or length - past sets device
+ * error SPECKV_DERR_PACKET and moves nothing. Replaces the host round trip
+ * between schedule (helper/opd_scheduling.py:5-32) and the commit at
+ * helper/opd_generate.py:632-650 (compaction loop, crop, position update). */
+int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_t layers,
+                        int64_t batch, int64_t heads, int64_t dim, int64_t capacity, int64_t length,
+                        int32_t elem_bytes, const int64_t* chosen, int64_t chosen_stride_b,
+                        int64_t chosen_stride_w, int64_t past, const int64_t* packet,
+                        int64_t packet_stride, int64_t max_width, uint8_t* pad_rows,
+                        int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
+                        uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
+                        int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
+                        int64_t* past_positions, void* stream);
 
 /* ---- KV rows: batch remap (repeat / select) ---------------------------- */
 
