@@ -528,7 +528,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
 //               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
 //               warpgroup works while the tensor pipe serves the other tile
-//   warps 2-5   softmax of row tile 0; warps 6-9 softmax of row tile 1: thread =
+//   warps 2-3   idle (they complete the first warpgroup for the register split)
+//   warps 4-7   softmax of row tile 0; warps 8-11 softmax of row tile 1: thread =
 //               row = TMEM lane (warp % 4 picks the lane quarter); S is read once
 //               into registers, P (16-bit) goes back into the first 64 columns of
 //               its S buffer and feeds the P.V MMA straight from TMEM.
@@ -536,7 +537,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // softmax warpgroup sees S_t,i complete, P_t,i-1 . V_i-1 has finished too: O_t
 // may be rescaled and the P region rewritten without further waits.
 // ---------------------------------------------------------------------------
-constexpr int kThreads2 = 320;
+constexpr int kThreads2 = 384;
+// Register split after the prologue (setmaxnreg): the producer / MMA warpgroup drops
+// to kRegsLow, the two softmax warpgroups rise to kRegsHigh. The block is launched
+// with kRegsLaunch per thread (the host checks the compiled count), and
+// 128 * kRegsLow + 256 * kRegsHigh == 384 * kRegsLaunch, so every increase is
+// covered by the decrease.
+constexpr int kRegsLaunch = 168, kRegsLow = 152, kRegsHigh = 176;
+static_assert(128 * kRegsLow + 256 * kRegsHigh == kThreads2 * kRegsLaunch, "register split must balance");
 constexpr int kMaxSortB = 1024;
 constexpr uint32_t Q2_OFF = 0;                    // Q tile t at Q2_OFF + t * kTileBytes
 constexpr uint32_t K2_OFF = 2 * kTileBytes;       // K stage s at K2_OFF + s * kTileBytes
@@ -550,6 +558,32 @@ __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t
 
 enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
        C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18 };
+
+// Warp-wide forms: every lane runs the same code (the operands stay warp-uniform) and
+// one elected lane, always lane 0 with the full mask, issues the instruction; the
+// commits are issued by that same lane, so they track its MMAs.
+__device__ __forceinline__ void tc_mma_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n .reg .b32 r;\n elect.sync r|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n .reg .b32 r;\n elect.sync r|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_w(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n .reg .b32 r;\n elect.sync r|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+      : "memory");
+}
 
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
@@ -705,6 +739,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
     return true;
   };
 
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
@@ -737,8 +773,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (whole warp, lane 0 issues) ----------------
+    {
       const uint32_t ab = TypeCode<T>::value;
       const uint32_t id_s = idesc_f16(ab, 0), id_pv = idesc_f16(ab, 1);
       int cnt = 0;            // key tiles consumed (global)
@@ -746,78 +782,82 @@ __global__ void __launch_bounds__(kThreads2, 1)
       int ic[2] = {0, 0};     // items per row tile
       bool ok = true;
       Item it;
+      auto wait = [&](int b, uint32_t parity, int where) {
+        return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, abort_flag, a.err, where));
+      };
       // Descriptor bases, computed once; a K step only adds a constant to the
       // start-address field (16-byte units): K-major +32 B per 16 elements inside a
-      // 128-byte swizzle atom and +16 KB per 64-element half, V (MN-major) +2 KB.
-      const uint64_t q_desc[2] = {sw128_desc(sbase + Q2_OFF, 16, 1024),
-                                  sw128_desc(sbase + Q2_OFF + kTileBytes, 16, 1024)};
-      const uint64_t k_desc[2] = {sw128_desc(sbase + K2_OFF, 16, 1024),
-                                  sw128_desc(sbase + K2_OFF + kTileBytes, 16, 1024)};
-      const uint64_t v_desc[2] = {sw128_desc(sbase + V2_OFF, kTileHalf, 1024),
-                                  sw128_desc(sbase + V2_OFF + kTileBytes, kTileHalf, 1024)};
+      // 128-byte swizzle atom and +16 KB per 64-element half, V (MN-major) +2 KB; a
+      // ring stage adds kTileBytes.
+      const uint64_t q_desc = sw128_desc(sbase + Q2_OFF, 16, 1024);
+      const uint64_t k_desc = sw128_desc(sbase + K2_OFF, 16, 1024);
+      const uint64_t v_desc = sw128_desc(sbase + V2_OFF, kTileHalf, 1024);
+      constexpr uint64_t kStageStep = kTileBytes >> 4;
       auto issue_s = [&](int t, int stage) {
-        const uint64_t ad = q_desc[t], bd = k_desc[stage];
+        const uint64_t ad = q_desc + (uint64_t)t * kStageStep, bd = k_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + S_COL(t);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t step = (uint64_t)((kk >> 2) * (kTileHalf >> 4) + (kk & 3) * 2);
-          tc_mma(d, ad + step, bd + step, id_s, kk > 0 ? 1u : 0u);
+          tc_mma_w(d, ad + step, bd + step, id_s, kk > 0 ? 1u : 0u);
         }
-        tc_commit(bar(C_S_FULL + t));
+        tc_commit_w(bar(C_S_FULL + t));
       };
       auto issue_pv = [&](int t, int stage, bool first) -> bool {
-        if (!mbar_wait(bar(C_P_FULL + t), sc[t] & 1, abort_flag, a.err, 23)) return false;
+        if (!wait(C_P_FULL + t, sc[t] & 1, 23)) return false;
         ++sc[t];
         tc_fence_after();
-        const uint64_t bd = v_desc[stage];
+        const uint64_t bd = v_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + O2_COL(t), pa = tmem + S_COL(t);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_ts(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, (!first || kk > 0) ? 1u : 0u);
+          tc_mma_ts_w(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, (!first || kk > 0) ? 1u : 0u);
         return true;
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
         const bool act1 = it.pair * 2 * BM + BM < total_rows;
         const int n = n_tiles_all - first_tile(it.b);
-        ok = mbar_wait(bar(C_Q_FULL + 0), ic[0] & 1, abort_flag, a.err, 24);
-        if (ok && act1) ok = mbar_wait(bar(C_Q_FULL + 1), ic[1] & 1, abort_flag, a.err, 25);
+        ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
+        if (ok && act1) ok = wait(C_Q_FULL + 1, ic[1] & 1, 25);
         tc_fence_after();
         int prev_stage = 0;
         for (int i = 0; ok && i < n; ++i, ++cnt) {
           const int s = cnt & 1;
-          if (!mbar_wait(bar(C_K_FULL + s), (cnt >> 1) & 1, abort_flag, a.err, 26)) { ok = false; break; }
+          if (!wait(C_K_FULL + s, (cnt >> 1) & 1, 26)) { ok = false; break; }
           tc_fence_after();
           issue_s(0, s);
           if (act1 && i > 0) {
             if (!issue_pv(1, prev_stage, i == 1)) { ok = false; break; }
-            tc_commit(bar(C_V_EMPTY + prev_stage));
+            tc_commit_w(bar(C_V_EMPTY + prev_stage));
           }
           if (act1) issue_s(1, s);
-          tc_commit(bar(C_K_EMPTY + s));
-          if (!mbar_wait(bar(C_V_FULL + s), (cnt >> 1) & 1, abort_flag, a.err, 27)) { ok = false; break; }
+          tc_commit_w(bar(C_K_EMPTY + s));
+          if (!wait(C_V_FULL + s, (cnt >> 1) & 1, 27)) { ok = false; break; }
           tc_fence_after();
           if (!issue_pv(0, s, i == 0)) { ok = false; break; }
-          if (!act1) tc_commit(bar(C_V_EMPTY + s));
+          if (!act1) tc_commit_w(bar(C_V_EMPTY + s));
           prev_stage = s;
         }
         if (ok && act1) {
-          if (issue_pv(1, prev_stage, n == 1)) tc_commit(bar(C_V_EMPTY + prev_stage));
+          if (issue_pv(1, prev_stage, n == 1)) tc_commit_w(bar(C_V_EMPTY + prev_stage));
           else ok = false;
         }
         if (!ok) break;
-        tc_commit(bar(C_O_FINAL + 0));
+        tc_commit_w(bar(C_O_FINAL + 0));
         ++ic[0];
         if (act1) {
-          tc_commit(bar(C_O_FINAL + 1));
+          tc_commit_w(bar(C_O_FINAL + 1));
           ++ic[1];
         }
       }
-      tc_commit(bar(C_DRAIN));  // every MMA of this thread completes before TMEM is released
+      tc_commit_w(bar(C_DRAIN));  // every MMA of lane 0 completes before TMEM is released
       drain_wait(bar(C_DRAIN), 0);
     }
-  } else if (warp >= 2) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ---------------- softmax warpgroups ----------------
-    const int t = (warp - 2) >> 2;                 // row tile of this warpgroup
+    const int t = (warp - 4) >> 2;                 // row tile of this warpgroup
     const int quarter = warp & 3;                  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;           // row within the tile == TMEM lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
@@ -1033,6 +1073,16 @@ int sm_count() {
 template <typename T>
 int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, cudaStream_t stream) {
   auto kern = attn_pair_kernel<T>;
+  // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
+  // per thread; any other count could leave the increase waiting for registers.
+  static int regs = -1;
+  if (regs < 0) {
+    cudaFuncAttributes fa;
+    regs = cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : 0;
+  }
+  if (regs != kRegsLaunch)
+    return fail(SPECKV_ENOSUPPORT, "speckv_tree_attention_bits: kernel compiled with %d registers per thread, "
+                "the register split needs %d", regs, kRegsLaunch);
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
   const long long pairs = ((long long)s.group * s.rows + 2 * BM - 1) / (2 * BM);
   const long long items = (long long)s.batch * s.kv_heads * pairs;
