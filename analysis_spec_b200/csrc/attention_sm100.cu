@@ -543,7 +543,7 @@ constexpr int kThreads2 = 384;
 // with kRegsLaunch per thread (the host checks the compiled count), and
 // 128 * kRegsLow + 256 * kRegsHigh == 384 * kRegsLaunch, so every increase is
 // covered by the decrease.
-constexpr int kRegsLaunch = 168, kRegsLow = 152, kRegsHigh = 176;
+constexpr int kRegsLaunch = 168, kRegsLow = 136, kRegsHigh = 184;
 static_assert(128 * kRegsLow + 256 * kRegsHigh == kThreads2 * kRegsLaunch, "register split must balance");
 constexpr int kMaxSortB = 1024;
 constexpr uint32_t Q2_OFF = 0;                    // Q tile t at Q2_OFF + t * kTileBytes
@@ -636,29 +636,33 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair of x <= 8 on the FMA pipe (relieves the MUFU ex2 unit, which
-// alone would need ~1 us per key tile for the two softmax warpgroups).
-// Range reduction 2^x = 2^n * 2^f, n = round(x) via the 1.5 * 2^23 addition,
-// f = x - n in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients are a
-// minimax fit of the relative error on [-0.5, 0.5] (linear program over 4001
-// points; max relative error 7.5e-5 in fp32 Horner form); 2^n is added to the
-// exponent field as an integer. Inputs at or below -126 (masked scores are
-// -inf) give exactly +0; the reduction runs on x clamped to -126 so the exponent
-// sum never leaves the float range.
+// 2^x for a pair on the FMA pipe (relieves the MUFU ex2 unit, which alone would
+// bound the softmax): x = n + f with n = rint(x) from the 1.5 * 2^23 shift, 2^f by a
+// degree-3 polynomial on [-0.5, 0.5] (minimax in relative error, fitted by linear
+// programming on 2049 points; max relative error 7.5e-5, below the 16-bit rounding
+// of P), and 2^n applied as one multiply by the float whose exponent field is n + 127.
+// x <= -127 (masked scores are -inf) gives exactly +0. Valid for x < 128; larger
+// arguments only occur in a tile that is recomputed against a larger reference.
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  const float2 xc = make_float2(fmaxf(x.x, -126.f), fmaxf(x.y, -126.f));
-  const float2 t = fadd2(xc, make_float2(kRound, kRound));
-  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
-  const float2 f = fadd2(xc, make_float2(-n.x, -n.y));
-  float2 p = ffma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111251f, 0.2426111251f));
-  p = ffma2(p, f, make_float2(0.6932609678f, 0.6932609678f));
-  p = ffma2(p, f, make_float2(0.9999280572f, 0.9999280572f));
-  // (bits(t) << 23) keeps exactly n << 23: the 0x4B400000 of the rounding constant shifts out
-  const float rx = __uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23));
-  const float ry = __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23));
-  return make_float2(x.x > -126.f ? rx : 0.f, x.y > -126.f ? ry : 0.f);
+  const float2 xc = make_float2(fmaxf(x.x, -127.f), fmaxf(x.y, -127.f));
+  const float2 t = __fadd2_rn(xc, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __fadd2_rn(xc, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111251f, 0.2426111251f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609678f, 0.6932609678f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  // bits(t) = 0x4B400000 + n, so (bits(t) + 127) << 23 == (n + 127) << 23 (mod 2^32): 2^n,
+  // and exactly 0 for n = -127
+  const float sx = __uint_as_float((__float_as_uint(t.x) + 127u) << 23);
+  const float sy = __uint_as_float((__float_as_uint(t.y) + 127u) << 23);
+  return __fmul2_rn(p, make_float2(sx, sy));
 }
+
+// Which 2-column pairs take the polynomial (1 in 4): moves a quarter of the exponentials
+// from the MUFU unit (16 results per clock per SM) to the FMA pipe (~15 issue slots per
+// pair); the measured optimum between all-MUFU and half-and-half.
+__host__ __device__ constexpr bool poly_pair(int q) { return (q & 7) == 1 || (q & 7) == 5; }
 
 struct Item {
   int b, kvh, pair;
@@ -941,14 +945,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
         float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                           make_float2(0.f, 0.f)};  // independent partial sums: no 64-long add chain
         // P = 2^(s * scale - m), packed to 16 bits over the first 64 columns of S;
-        // half of the pairs on the MUFU ex2 unit, half by polynomial on the FMA pipe
+        // pairs on the MUFU ex2 unit or by polynomial on the FMA pipe (poly_pair)
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           uint32_t pk[8];
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
             float2 e = __ffma2_rn(make_float2(x[cc * 16 + j], x[cc * 16 + j + 1]), sc2, neg);
-            if ((j >> 1) & 1) {
+            if (poly_pair(j >> 1)) {
               e = exp2_poly2(e);
             } else {
               e.x = ex2(e.x);
