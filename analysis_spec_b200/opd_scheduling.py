@@ -69,12 +69,14 @@ def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
     plugin.pad_schedule(path, past, eos, tokens, indices, mask, last, out_packet, snapshot=snapshot)
     if commit is not None:
         commit(tokens, indices, mask, out_packet)
+    # whole rows of the packet buffer: one contiguous copy, no gather kernel before the D2H
+    host = packet[:b].cpu() if packet.is_contiguous() else packet[:b, :capacity + 4].cpu()
     if reflex:
-        rows = packet[:b, :capacity + 4].cpu().tolist()
+        rows = host[:, :capacity + 4].tolist()
         opd.host_active_count = rows[0][-1]
         rows = [row[:-1] for row in rows]
     else:
-        rows = out_packet.cpu().tolist()
+        rows = host[:, :capacity + 3].tolist()
     width = max(row[0] for row in rows)
     if kernels is None:
         rows = [row[:3 + width] for row in rows]
