@@ -77,6 +77,19 @@ def peaks():
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
 
 
+def dram_traffic(entry, layers):
+    """DRAM bytes per launch of one of this path's kernels from the committed ncu capture
+    (scaled to `layers` where the traffic grows with the layer count), or None."""
+    path = ROOT / 'profiles' / 'dram_traffic_qwen25_3b.json'
+    if not path.exists():
+        return None
+    k = json.loads(path.read_text())['kernels'].get(entry)
+    if k is None:
+        return None
+    per = k['dram_read_bytes'] + k['dram_write_bytes']
+    return int(per * (layers / k['captured_layers'] if k['scale'] != 1.0 else 1.0))
+
+
 def workload_config(wl, extra=None):
     cfg = {'workload': f'{wl.name}: {wl.layers} layers, batch {wl.batch}, {wl.q_heads}q/{wl.kv_heads}kv heads x '
                        f'{wl.dim}, {wl.dtype}, max_len {wl.capacity}, prefix {wl.prefix}, {wl.nodes}-node tree '
@@ -91,17 +104,48 @@ def workload_config(wl, extra=None):
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class Clocks:
-    """nvidia-smi samples (every 20 ms) of this GPU's SM clock and throttle reasons."""
+    """SM clock and clock-event reasons of this GPU sampled during the timed region: NVML
+    every 5 ms from a background thread (read-only queries), nvidia-smi every 20 ms when the
+    NVML binding is unavailable."""
     FIELDS = ('uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+    NAMES = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
 
     def __init__(self, uuid):
         self.uuid = str(uuid).lower().replace('gpu-', '')
         self.proc = None
         self.file = None
+        self.thread = None
+        self.samples = []
+        self.max_mhz = 0.0
 
     def start(self):
+        try:
+            import threading
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByUUID('GPU-' + self.uuid)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            bits = (pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM))
+                        mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                        self.samples.append((mhz, {n for n, bit in zip(self.NAMES, bits) if mask & bit}))
+                    except pynvml.NVMLError:
+                        pass
+                    self._stop.wait(0.005)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
             self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
@@ -110,6 +154,15 @@ class Clocks:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            if not self.samples:
+                return None
+            sm = [m for m, _ in self.samples]
+            reasons = set().union(*(r for _, r in self.samples))
+            return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': self.max_mhz, 'samples': len(sm),
+                    'reasons': sorted(reasons), 'source': 'nvml'}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -126,19 +179,19 @@ class Clocks:
         elif len(uuids) != 1:
             return None
         sm, mx, reasons = [], 0.0, set()
-        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
         for r in rows:
             try:
                 sm.append(float(r[1]))
                 mx = max(mx, float(r[2]))
-                for name, flag in zip(names, r[5:9]):
+                for name, flag in zip(self.NAMES, r[5:9]):
                     if flag.strip().lower() in ('active', '1'):
                         reasons.add(name)
             except (ValueError, IndexError):
                 continue
         if not sm:
             return None
-        return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': mx, 'samples': len(sm), 'reasons': sorted(reasons)}
+        return {'sm_mhz': float(np.median(sm)), 'sm_max_mhz': mx, 'samples': len(sm), 'reasons': sorted(reasons),
+                'source': 'nvidia-smi'}
 
 
 # ---------------------------------------------------------------------------
@@ -341,9 +394,11 @@ def run_ours(args):
                         'attention_tflops': round(attn_tflops, 2),
                         'roofline': {'bound': 'tensor', 'achieved': round(attn_tflops, 2), 'peak': tflops,
                                      'unit': 'TFLOP/s', 'frac': round(attn_tflops / tflops, 4),
-                                     'traffic': None, 'peak_kind': peak_kind}},
+                                     'traffic': dram_traffic('speckv_tree_attention_bits', wl.layers),
+                                     'peak_kind': peak_kind}},
         'roofline': {'bound': 'hbm', 'kernel': 'speckv_append_rows (all layers)', 'achieved': round(append_gbs, 1),
-                     'peak': hbm, 'unit': 'GB/s', 'frac': round(append_gbs / hbm, 4), 'traffic': None,
+                     'peak': hbm, 'unit': 'GB/s', 'frac': round(append_gbs / hbm, 4),
+                     'traffic': dram_traffic('speckv_append_rows', wl.layers),
                      'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
         'gpu_launches': launches,

@@ -1,0 +1,105 @@
+"""The drop-in on a real transformers model: a small random-weight Qwen2 (head_dim 128, GQA
+4 q / 2 KV heads, bf16) prefills left-padded prompts into OPDStaticCache, then runs the tree
+verify forward with the reference's 4-D additive tree mask
+(helper/opd_generate.py:470-495) three ways: transformers' SDPA (the reference path), the
+registered 'speckv_tree' attention on the dense mask, and on the visibility bits attached to
+the mask. Logits must agree within bf16 tolerance and greedy acceptance must be identical."""
+import numpy as np
+import pytest
+import torch
+
+from analysis_spec_b200 import _ops, tree_kernels, workloads as W
+from analysis_spec_b200.opd_scheduling import schedule
+from analysis_spec_b200.opd_static_cache import OPDStaticCache
+from analysis_spec_b200.tree_attention import register
+from analysis_spec_b200.tree_verification import PackedTree, trace_verified_path
+
+pytestmark = pytest.mark.gpu
+
+VOCAB, B, PROMPT, ROWS, DEPTH, TOPK = 512, 4, 16, 13, 4, 3
+
+
+def _model():
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=VOCAB, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=512,
+                      rms_norm_eps=1e-6, tie_word_embeddings=False)
+    cfg._attn_implementation = 'sdpa'
+    return Qwen2ForCausalLM(cfg).to('cuda', torch.bfloat16).eval()
+
+
+def _inputs():
+    rng = np.random.RandomState(3)
+    lengths = np.array([5, 9, 12, 16])
+    ids = rng.randint(0, VOCAB, size=(B, PROMPT))
+    mask2d = np.zeros((B, PROMPT), dtype=np.int64)
+    for b, n in enumerate(lengths):
+        mask2d[b, PROMPT - n:] = 1
+    parents, tokens = W.packed_trees(rng, B, ROWS - 1, DEPTH, TOPK, vocab=VOCAB)
+    tokens[:, 0] = rng.randint(0, VOCAB, size=B)  # root = last committed token
+    depth = np.zeros_like(parents)
+    for r in range(1, ROWS):
+        depth[:, r] = depth[np.arange(B), parents[:, r]] + 1
+    positions = lengths[:, None] + depth  # the root follows the last prompt token
+    return ids, mask2d, parents, tokens, positions
+
+
+def _prefill(model, ids, mask2d):
+    cache = OPDStaticCache(64, batch_capacity=B)
+    am = torch.from_numpy(mask2d).cuda()
+    pos = (am.cumsum(-1) - 1).clamp(min=0)
+    with torch.no_grad():
+        model(input_ids=torch.from_numpy(ids).cuda(), attention_mask=am, position_ids=pos, past_key_values=cache,
+              use_cache=True)
+    return cache
+
+
+def _verify(model, cache, tree, tokens, positions, mask, impl):
+    model.config._attn_implementation = impl
+    for layer in model.model.layers:
+        layer.self_attn.config._attn_implementation = impl
+    with torch.no_grad():
+        out = model(input_ids=torch.from_numpy(tokens).cuda(), attention_mask=mask,
+                    position_ids=torch.from_numpy(positions).cuda(), past_key_values=cache, use_cache=True)
+    return out.logits.float()
+
+
+def test_tree_verify_forward_matches_sdpa_and_greedy_acceptance():
+    name = register()
+    model = _model()
+    ids, mask2d, parents, tokens, positions = _inputs()
+    pad_np = np.zeros((B, PROMPT + ROWS), dtype=bool)
+    pad_np[:, :PROMPT] = mask2d == 0
+    pad = torch.from_numpy(pad_np).cuda()
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(tokens).cuda(),
+                      torch.zeros(B, ROWS, dtype=torch.long, device='cuda'), DEPTH)
+    results = {}
+    for impl in ('sdpa', 'dense', 'bits'):
+        cache = _prefill(model, ids, mask2d)
+        assert cache.get_seq_length() == PROMPT
+        mask = tree.attention_mask(PROMPT, torch.bfloat16, pad)
+        if impl == 'bits':
+            mask = tree.visibility(PROMPT, pad).attach(mask)
+        logits = _verify(model, cache, tree, tokens, positions, mask, 'sdpa' if impl == 'sdpa' else name)
+        assert cache.get_seq_length() == PROMPT + ROWS
+        results[impl] = logits
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+    ref = results['sdpa']
+    scale = ref.abs().max().item()
+    for impl in ('dense', 'bits'):
+        err = (results[impl] - ref).abs()
+        assert err.max().item() <= 2e-2 * max(scale, 1.0), (impl, err.max().item(), scale)
+        assert err.mean().item() <= 2e-3 * max(scale, 1.0), (impl, err.mean().item(), scale)
+    # greedy acceptance: samples = argmax of each row's logits, traced through the tree
+    eos = VOCAB + 1
+    lengths = {}
+    for impl, logits in results.items():
+        samples = logits.argmax(-1)
+        path = trace_verified_path(tree, samples, eos)
+        rows, *_ = schedule(path, PROMPT, eos, None, None, tree_kernels)
+        lengths[impl] = [r[0] for r in rows]
+    agree = (results['bits'].argmax(-1) == ref.argmax(-1)).float().mean().item()
+    assert agree >= 0.95, agree
+    assert lengths['dense'] == lengths['sdpa'] and lengths['bits'] == lengths['sdpa'], lengths
