@@ -10,10 +10,10 @@ accumulates after every verification (helper/opd_generate.py:551-555):
     verified_rows   += 1                    per row   (avg_acc_length[1])
     finished_rows   += eos flag of the row's packet
 
-The all_reduce of round i is issued on a side stream and waited for at round
-i + 1, so it never sits between two KV kernels. NCCL (CUDA tensors) and gloo
-(CPU tensors) both work; a rank that fails surfaces on the others as an error
-from their next `add_round`/`finish` once the process group's timeout expires.
+The all_reduce of each round runs on a side stream, so it never sits between
+two KV kernels and never blocks the host. NCCL (CUDA tensors) and gloo (CPU
+tensors) both work; a rank that fails surfaces on the others as an error from
+their next `add_round`/`finish` once the process group's timeout expires.
 """
 import torch
 
@@ -30,7 +30,13 @@ def round_increments(rows, proposed_per_row):
 
 
 class AcceptanceCounters:
-    """Job-wide totals of `FIELDS`; `total` holds every reduction that has completed."""
+    """Job-wide totals of `FIELDS`.
+
+    On CUDA the reduced vectors are accumulated on the device by the side stream (the
+    all_reduce's completion is awaited by that stream, never by the host), so rounds do not
+    synchronise the ranks' hosts; `finish` reads the totals back once. With CPU tensors
+    (gloo) the previous round's reduction is awaited when the next one is queued.
+    """
 
     def __init__(self, device, group=None):
         import torch.distributed as dist
@@ -40,36 +46,41 @@ class AcceptanceCounters:
         self.total = torch.zeros(len(FIELDS), dtype=torch.long)
         self._work = None
         self._vec = None
-        self._stream = torch.cuda.Stream(self.device) if self.device.type == 'cuda' and self.distributed else None
+        self._cuda = self.device.type == 'cuda'
+        self._stream = torch.cuda.Stream(self.device) if self._cuda else None
+        self._total_dev = torch.zeros(len(FIELDS), dtype=torch.long, device=self.device) if self._cuda else None
 
     def _collect(self):
         if self._work is not None:
             self._work.wait()
-            if self._stream is not None:
-                torch.cuda.current_stream(self.device).wait_stream(self._stream)
-            self.total += self._vec.cpu()
+            self.total += self._vec
             self._work = None
             self._vec = None
 
     def add_round(self, values):
-        """Queues the reduction of this round's increments and folds in the previous round's."""
+        """Queues the reduction of this round's increments."""
         import torch.distributed as dist
-        self._collect()
         vec = torch.tensor(values, dtype=torch.long)
-        if not self.distributed:
-            self.total += vec
-            return
-        if self._stream is not None:
+        if self._cuda:
             vec = vec.pin_memory().to(self.device, non_blocking=True)
             self._stream.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self._stream):
                 vec.record_stream(self._stream)
-                self._work = dist.all_reduce(vec, group=self.group, async_op=True)
-        else:
-            self._work = dist.all_reduce(vec, group=self.group, async_op=True)
+                if self.distributed:
+                    dist.all_reduce(vec, group=self.group, async_op=True).wait()  # the side stream waits
+                self._total_dev.add_(vec)
+            return
+        self._collect()
+        if not self.distributed:
+            self.total += vec
+            return
+        self._work = dist.all_reduce(vec, group=self.group, async_op=True)
         self._vec = vec
 
     def finish(self):
-        """Waits for the outstanding reduction and returns the totals as a dict."""
+        """Waits for the outstanding reductions and returns the totals as a dict."""
+        if self._cuda:
+            self._stream.synchronize()
+            return dict(zip(FIELDS, (self.total + self._total_dev.cpu()).tolist()))
         self._collect()
         return dict(zip(FIELDS, self.total.tolist()))
