@@ -288,6 +288,95 @@ __global__ void __launch_bounds__(kMaskThreads) tree_bits_kernel(const int64_t* 
 }
 
 // ---------------------------------------------------------------------------
+// bit-packed visibility, CTA per sequence: the prefix words (columns 0 .. past,
+// padding removed) are built once and shared by every row; each row adds its
+// ancestors as a bitstring over the tree columns past .. past + rows - 1. Same
+// words as tree_bits_kernel; no atomics (first_col is row 0's first visible column).
+// ---------------------------------------------------------------------------
+constexpr int kSeqBitsThreads = 256;
+constexpr long long kSeqBitsMaxRows = 256;  // rows x ceil(rows / 32) ancestor words in shared memory
+
+// bits [off, off + 32) of a bitstring of n words (bits outside it read as 0)
+__device__ __forceinline__ uint32_t bit_window(const uint32_t* a, int n, long long off) {
+  if (off <= -32 || off >= 32ll * n) return 0u;
+  const long long q = off >= 0 ? off / 32 : -((31 - off) / 32);
+  const int sh = (int)(off - 32 * q);
+  const uint32_t lo = (q >= 0 && q < n) ? a[q] : 0u;
+  const uint32_t hi = (q + 1 >= 0 && q + 1 < n) ? a[q + 1] : 0u;
+  return sh == 0 ? lo : (lo >> sh) | (hi << (32 - sh));
+}
+
+__global__ void __launch_bounds__(kSeqBitsThreads) tree_bits_seq_kernel(
+    const int64_t* __restrict__ parents, long long rows, long long past, long long steps,
+    const uint8_t* __restrict__ pad, long long pad_sb, uint32_t* bits, long long row_words, int* first_col,
+    unsigned long long* err) {
+  extern __shared__ __align__(16) unsigned char seq_smem[];
+  const int tw = (int)((rows + 31) / 32);                     // words of a tree bitstring
+  long long* par = reinterpret_cast<long long*>(seq_smem);    // [rows]
+  uint32_t* prefix = reinterpret_cast<uint32_t*>(par + rows);  // [row_words]
+  uint32_t* tree = prefix + row_words;                         // [rows][tw]
+  uint32_t* padt = tree + rows * tw;                           // [tw] padding of the tree columns
+  const long long b = blockIdx.x;
+  const long long cols = past + rows;
+  const uint8_t* prow = pad != nullptr ? pad + b * pad_sb : nullptr;
+  for (long long i = threadIdx.x; i < rows; i += kSeqBitsThreads) par[i] = parents[b * rows + i];
+  for (long long i = threadIdx.x; i < rows * tw; i += kSeqBitsThreads) tree[i] = 0u;
+  for (long long i = threadIdx.x; i < tw; i += kSeqBitsThreads) {
+    uint32_t word = 0;
+    for (int j = 0; j < 32; ++j) {
+      const long long t = i * 32 + j;
+      if (t < rows && prow != nullptr && prow[past + t]) word |= 1u << j;
+    }
+    padt[i] = word;
+  }
+  // prefix: column c <= past is visible unless padded (c == past is the root)
+  for (long long w = threadIdx.x; w < row_words; w += kSeqBitsThreads) {
+    uint32_t word = 0;
+    const long long c0 = w * 32;
+    for (int j = 0; j < 32; ++j) {
+      const long long c = c0 + j;
+      if (c > past) break;
+      if (prow == nullptr || !prow[c]) word |= 1u << j;
+    }
+    prefix[w] = word;
+  }
+  __syncthreads();
+  // ancestors of row r (itself included) within `steps` parent hops
+  for (long long r = threadIdx.x; r < rows; r += kSeqBitsThreads) {
+    uint32_t* tr = tree + r * tw;
+    long long cur = r;
+    for (long long k = 0; k < steps; ++k) {
+      if (cur >= 0) tr[cur >> 5] |= 1u << (cur & 31);
+      const long long at = cur > 0 ? cur : 0;
+      if (at >= rows) {
+        record_error(err, SPECKV_DERR_TREE_INDEX, at);
+        break;
+      }
+      cur = par[at];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int fc = 0x7f7f7f7f;
+    for (long long w = 0; w < row_words; ++w)
+      if (prefix[w] != 0u) {
+        fc = (int)(w * 32 + __ffs(prefix[w]) - 1);
+        break;
+      }
+    first_col[b] = fc;
+  }
+  const uint32_t rw = (uint32_t)row_words, total = (uint32_t)(rows * row_words);  // < 2^31: checked on the host
+  for (uint32_t idx = threadIdx.x; idx < total; idx += kSeqBitsThreads) {
+    const uint32_t r = idx / rw, w = idx - r * rw;
+    const long long off = (long long)w * 32 - past;  // tree column offset of the word's first bit
+    uint32_t word = prefix[w];
+    if (off > -32 && off < rows) word |= bit_window(tree + r * tw, tw, off) & ~bit_window(padt, tw, off);
+    if ((long long)w * 32 >= cols) word = 0u;
+    bits[b * rows * row_words + idx] = word;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // position / padding update: one warp per sequence.
 // ---------------------------------------------------------------------------
 __global__ void position_update_kernel(PositionArgs a, long long batch, long long past, long long width,
@@ -424,6 +513,15 @@ extern "C" int speckv_tree_mask_bits(const int64_t* parents, int64_t batch, int6
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long tw = (rows + 31) / 32;
+  const long long seq_smem = rows * 8 + (row_words + rows * tw + tw) * 4;
+  if (rows <= kSeqBitsMaxRows && seq_smem <= 200 * 1024 && rows * row_words < (1ll << 31)) {
+    if (seq_smem > 48 * 1024)
+      cudaFuncSetAttribute(tree_bits_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)seq_smem);
+    tree_bits_seq_kernel<<<(unsigned)batch, kSeqBitsThreads, (size_t)seq_smem, s>>>(
+        parents, rows, past, steps, pad, pad_stride_b, bits, row_words, first_col, err);
+    return check_launch(fn);
+  }
   // 0x7f7f7f7f: larger than any column, lowered by atomicMin in the kernel
   cudaError_t e = cudaMemsetAsync(first_col, 0x7f, (size_t)batch * sizeof(int32_t), s);
   if (e != cudaSuccess) return fail(SPECKV_ECUDA, "%s: %s", fn, cudaGetErrorString(e));

@@ -102,6 +102,29 @@ def test_visibility_bits_match_mask_rule():
         assert np.array_equal(vis.first_col.cpu().numpy(), first)
 
 
+def test_visibility_bits_scattered_padding():
+    # padding committed in earlier rounds is scattered through the prefix (gap-first
+    # schedules), and the pad bitmap may cover tree columns too (never the root)
+    rng = np.random.RandomState(12)
+    for batch, rows, past, depth in ((5, 61, 333, 6), (3, 40, 31, 9), (2, 255, 64, 30)):
+        parents = np.full((batch, rows), -1, dtype=np.int64)
+        for b in range(batch):
+            for r in range(1, rows):
+                parents[b, r] = rng.randint(max(0, r - 7), r)
+        pad = rng.rand(batch, past + rows) < 0.3
+        pad[:, past] = False
+        pad[:, past + 1:] &= rng.rand(batch, rows - 1) < 0.5
+        tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(parents).cuda(),
+                          torch.from_numpy(parents).cuda(), depth)
+        vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+        bits = vis.bits.cpu().numpy().view(np.uint32)
+        unpacked = np.unpackbits(bits.view(np.uint8), bitorder='little').reshape(batch, rows, -1)
+        expect = oracle.tree_visible(parents, past, depth + 1, pad=pad)
+        assert np.array_equal(unpacked[:, :, :past + rows].astype(bool), expect)
+        assert not unpacked[:, :, past + rows:].any()
+        assert np.array_equal(vis.first_col.cpu().numpy(), expect[:, 0].argmax(axis=1))
+
+
 @pytest.mark.parametrize('batch,hq,hkv,rows,past,ragged', [(4, 16, 2, 61, 700, True), (3, 28, 4, 61, 300, True),
                                                           (2, 40, 8, 61, 260, True), (2, 16, 2, 17, 3000, True),
                                                           (1, 16, 2, 1, 129, False), (5, 8, 2, 33, 127, False)])
