@@ -385,6 +385,34 @@ class OPDStaticCache(Cache):
         self.kv_rows_moved += count
 
     # ---- B200 additions ----------------------------------------------------------
+    def admit(self, key_states, value_states):
+        """Writes the prefixes of k new sequences into rows [batch, batch + k) of every layer.
+
+        ``key_states[l]`` / ``value_states[l]`` are (k, heads, length, dim), already
+        left-padded to the cache's shared length; all layers are written in one launch
+        and the live batch grows by k. Refills the rows ``swap_remove`` released; the
+        reference has no admission step of its own (its rollouts start full).
+        """
+        layers = self.layers[:len(key_states)]
+        if not layers or len(key_states) != len(value_states) or len(layers) != len(self.layers):
+            raise ValueError('one key and one value tensor per layer required')
+        count = key_states[0].shape[0]
+        length = layers[0].length
+        if any(l.length != length or l.batch_size != layers[0].batch_size for l in layers):
+            raise ValueError('admission needs every layer at one length and batch size')
+        if key_states[0].shape[-2] != length:
+            raise ValueError('admitted prefixes must be left-padded to the cache length')
+        if count == 0:
+            return
+        start = layers[0].batch_size
+        for layer in layers:
+            layer._grow(max(length, 1), batch_needed=start + count)
+        if length:
+            _ops.append_rows([l.key_pool[start:] for l in layers], [l.value_pool[start:] for l in layers],
+                             list(key_states), list(value_states), 0)
+        for layer in layers:
+            layer.batch_size = start + count
+
     def update_layers(self, key_states, value_states):
         """Appends key_states[l] / value_states[l] to layer l for every l in one launch.
 
