@@ -578,6 +578,14 @@ __device__ __forceinline__ void tc_mma_ts_w(uint32_t d_tmem, uint32_t a_tmem, ui
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// true on one lane of the (converged) warp, the same lane every time with the full mask
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred p;\n .reg .b32 r;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ void tc_commit_w(uint32_t bar) {
   asm volatile(
       "{\n .reg .pred e;\n .reg .b32 r;\n elect.sync r|e, 0xffffffff;\n"
@@ -797,15 +805,21 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const uint64_t k_desc = sw128_desc(sbase + K2_OFF, 16, 1024);
       const uint64_t v_desc = sw128_desc(sbase + V2_OFF, kTileHalf, 1024);
       constexpr uint64_t kStageStep = kTileBytes >> 4;
+      // descriptors are computed by the whole warp (warp-uniform); one elected lane issues
+      // the group of MMAs and its commit
       auto issue_s = [&](int t, int stage) {
         const uint64_t ad = q_desc + (uint64_t)t * kStageStep, bd = k_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + S_COL(t);
+        const uint32_t sbar = bar(C_S_FULL + t);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t step = (uint64_t)((kk >> 2) * (kTileHalf >> 4) + (kk & 3) * 2);
-          tc_mma_w(d, ad + step, bd + step, id_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint64_t step = (uint64_t)((kk >> 2) * (kTileHalf >> 4) + (kk & 3) * 2);
+            tc_mma(d, ad + step, bd + step, id_s, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(sbar);
         }
-        tc_commit_w(bar(C_S_FULL + t));
+        __syncwarp();
       };
       auto issue_pv = [&](int t, int stage, bool first) -> bool {
         if (!wait(C_P_FULL + t, sc[t] & 1, 23)) return false;
@@ -813,9 +827,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tc_fence_after();
         const uint64_t bd = v_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + O2_COL(t), pa = tmem + S_COL(t);
+        const uint32_t acc0 = first ? 0u : 1u;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_ts_w(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, (!first || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk)
+            tc_mma_ts(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, kk > 0 ? 1u : acc0);
+        }
+        __syncwarp();
         return true;
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
