@@ -39,8 +39,12 @@ def _chunks(n):
         yield start, min(n, start + _lib.MAX_LAYERS)
 
 
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length):
-    """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers)."""
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True):
+    """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers).
+
+    With ``launch=False`` the arguments are validated and marshalled now and a callable
+    that issues the launches is returned, so the host work can run while the GPU is
+    still busy with earlier launches."""
     k0, v0 = key_srcs[0], value_srcs[0]
     _require_cuda(key_pools[0], k0)
     bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
@@ -58,12 +62,25 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length):
     ks =_lib.i64_array(k0.stride()[:3])
     vs = _lib.i64_array(v0.stride()[:3])
     es = key_pools[0].element_size()
-    for a, b in _chunks(len(key_pools)):
-        _lib.call('speckv_append_rows', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
-                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]),
-                  _lib.ptr_array([s.data_ptr() for s in key_srcs[a:b]]),
-                  _lib.ptr_array([s.data_ptr() for s in value_srcs[a:b]]),
-                  b - a, batch, heads, rows, dim, capacity, length, ks, vs, es, _stream(k0))
+    stream = _stream(k0)
+    calls = [(_lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+              _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]),
+              _lib.ptr_array([s.data_ptr() for s in key_srcs[a:b]]),
+              _lib.ptr_array([s.data_ptr() for s in value_srcs[a:b]]),
+              b - a, batch, heads, rows, dim, capacity, length, ks, vs, es, stream)
+             for a, b in _chunks(len(key_pools))]
+    return _issue('speckv_append_rows', calls, launch)
+
+
+def _issue(name, calls, launch):
+    """Issues prepared entry-point calls now, or returns a callable that issues them."""
+    def go():
+        for args in calls:
+            _lib.call(name, *args)
+    if launch:
+        go()
+        return None
+    return go
 
 
 def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width):
@@ -83,12 +100,13 @@ def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extensio
 
 
 def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, newly_padded=None, positions=None,
-                 past_positions=None, pad_rows=None, owners=None, pad_live=None):
+                 past_positions=None, pad_rows=None, owners=None, pad_live=None, launch=True):
     """Compaction of every layer + position/padding update of one verify round in one launch,
     with width and extension taken from the device packet (no host round trip).
 
     `chosen` / `newly_padded` / `positions` are full-width (batch, max_width) schedule outputs.
-    Pass no pools to update positions only, no `positions` to compact only.
+    Pass no pools to update positions only, no `positions` to compact only. With
+    ``launch=False`` returns a callable that issues the prepared launch (see append_rows).
     """
     key_pools = list(key_pools or [])
     _require_cuda(packet, chosen, newly_padded, positions, past_positions, pad_rows, owners, pad_live,
@@ -113,7 +131,7 @@ def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, ne
         if owners is not None:
             owners = _contig_long('owners', owners)
     if not widths:
-        return
+        return _issue('speckv_commit_round', [], launch)
     max_width = min(widths)
     pos_args = (_ptr(pad_rows), 0 if pad_rows is None else pad_rows.stride(0),
                 0 if pad_rows is None else pad_rows.shape[0], _ptr(owners), _ptr(pad_live),
@@ -123,16 +141,17 @@ def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, ne
     no_pos = (None, 0, 0, None, None, 0, None, 0, None, 0, None)
     stream = _stream(packet)
     if not key_pools:
-        _lib.call('speckv_commit_round', None, None, 0, batch, 1, 1, 1, 0, 1, None, 0, 0, past, packet.data_ptr(),
-                  packet.stride(0), max_width, *pos_args, stream)
-        return
+        return _issue('speckv_commit_round', [(None, None, 0, batch, 1, 1, 1, 0, 1, None, 0, 0, past,
+                                               packet.data_ptr(), packet.stride(0), max_width, *pos_args, stream)],
+                      launch)
     _, heads, capacity, dim = _pool_geometry(key_pools[0])
     es = key_pools[0].element_size()
-    for a, b in _chunks(len(key_pools)):
-        _lib.call('speckv_commit_round', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
-                  _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim, capacity,
-                  length, es, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, packet.data_ptr(),
-                  packet.stride(0), max_width, *(pos_args if a == 0 else no_pos), stream)
+    calls = [(_lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
+              _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim, capacity,
+              length, es, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, packet.data_ptr(),
+              packet.stride(0), max_width, *(pos_args if a == 0 else no_pos), stream)
+             for a, b in _chunks(len(key_pools))]
+    return _issue('speckv_commit_round', calls, launch)
 
 
 def remap_scratch_elements(new_batch, heads, dim, length, element_size):

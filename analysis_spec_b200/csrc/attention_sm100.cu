@@ -1123,6 +1123,8 @@ bool sm100_supported(const AttnArgs& a) {
       if ((st[i] * 2) % 16 != 0) return false;
   if (((uintptr_t)a.q | (uintptr_t)a.k | (uintptr_t)a.v | (uintptr_t)a.out) % 16 != 0) return false;
   if (a.batch > (1 << 20) || a.kv_len > (1 << 30)) return false;
+  // visibility words are read 16 bytes at a time
+  if (a.bits != nullptr && (a.row_words % 4 != 0 || (uintptr_t)a.bits % 16 != 0)) return false;
   return true;
 }
 

@@ -36,8 +36,11 @@ def schedule_commit(path, past, eos, workspace, packet, cache, positions, past_p
     (helper/opd_generate.py:632-650); returns ``schedule``'s tuple.
     """
     def commit(tokens, indices, mask, out_packet):
-        cache.commit_scheduled(indices, past, out_packet, newly_padded=mask, positions=positions,
-                               past_positions=past_positions, pad_rows=pad_rows, owners=owners, pad_live=pad_live)
+        # prepared before the schedule kernel is launched and issued right after it, so the
+        # host work of the commit overlaps the schedule kernel
+        return cache.commit_scheduled(indices, past, out_packet, newly_padded=mask, positions=positions,
+                                      past_positions=past_positions, pad_rows=pad_rows, owners=owners,
+                                      pad_live=pad_live, deferred=True)
 
     result = _schedule(path, past, eos, workspace, packet, kernels, opd, commit)
     cache.crop(past + result[5])
@@ -66,9 +69,10 @@ def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
     if reflex:
         snapshot = (opd.dispatch_snapshot if getattr(opd, 'async_updates', False)
                     else getattr(opd, 'dispatch_count', opd.active_count))
+    launch = commit(tokens, indices, mask, out_packet) if commit is not None else None
     plugin.pad_schedule(path, past, eos, tokens, indices, mask, last, out_packet, snapshot=snapshot)
-    if commit is not None:
-        commit(tokens, indices, mask, out_packet)
+    if launch is not None:
+        launch()
     # whole rows of the packet buffer: one contiguous copy, no gather kernel before the D2H
     host = packet[:b].cpu() if packet.is_contiguous() else packet[:b, :capacity + 4].cpu()
     if reflex:

@@ -413,11 +413,14 @@ class OPDStaticCache(Cache):
         for layer in layers:
             layer.batch_size = start + count
 
-    def update_layers(self, key_states, value_states):
+    def update_layers(self, key_states, value_states, deferred=False):
         """Appends key_states[l] / value_states[l] to layer l for every l in one launch.
 
         Same result as calling ``update(key_states[l], value_states[l], l)`` for each
-        layer; returns the per-layer (keys, values) views.
+        layer; returns the per-layer (keys, values) views. With ``deferred=True`` the
+        checks, growth and argument marshalling happen now and a callable is returned
+        that issues the launch and returns the views; call it before any other change
+        to this cache (it lets a caller overlap this host work with a running kernel).
         """
         if len(key_states) != len(value_states):
             raise ValueError('one key and one value tensor per layer required')
@@ -426,14 +429,21 @@ class OPDStaticCache(Cache):
             prepared.append(self._layer(idx)._prepare_append(k, v))
         layers = self.layers[:len(prepared)]
         if _uniform(layers):
-            _ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers],
-                             [p[0] for p in prepared], [p[1] for p in prepared], layers[0].length)
+            launches = [_ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers],
+                                         [p[0] for p in prepared], [p[1] for p in prepared], layers[0].length,
+                                         launch=False)]
         else:
-            for layer, (k, v, _) in zip(layers, prepared):
-                _ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length)
-        for layer, (_, _, end) in zip(layers, prepared):
-            layer.length = end
-        return LayerViews(layers)
+            launches = [_ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length, launch=False)
+                        for layer, (k, v, _) in zip(layers, prepared)]
+
+        def launch():
+            for go in launches:
+                go()
+            for layer, (_, _, end) in zip(layers, prepared):
+                layer.length = end
+            return LayerViews(layers)
+
+        return launch if deferred else launch()
 
     def commit_accepted(self, chosen, past, extension):
         """Accepted-path commit of every layer in one launch, then crop.
@@ -455,27 +465,35 @@ class OPDStaticCache(Cache):
         self.crop(past + width)
 
     def commit_scheduled(self, chosen, past, packet, newly_padded=None, positions=None, past_positions=None,
-                         pad_rows=None, owners=None, pad_live=None):
+                         pad_rows=None, owners=None, pad_live=None, deferred=False):
         """``commit_accepted`` with width and extension read from the device packet.
 
         ``chosen`` (and the position operands) are the full-width schedule
         outputs; the launch needs no host value of the round, so it can be
         enqueued before the packet is read back. The caller crops the cache to
-        ``past + width`` once it knows the width.
+        ``past + width`` once it knows the width. With ``deferred=True`` the
+        launch is prepared now (the operands' contents may still be written by
+        kernels enqueued later) and a callable that issues it is returned.
         """
         layers = [l for l in self.layers if l.key_pool is not None]
         pos = dict(newly_padded=newly_padded, positions=positions, past_positions=past_positions,
                    pad_rows=pad_rows, owners=owners, pad_live=pad_live)
         if not layers:
-            _ops.commit_round([], [], packet.shape[0], 0, chosen, past, packet, **pos)
+            launches = [_ops.commit_round([], [], packet.shape[0], 0, chosen, past, packet, **pos, launch=False)]
         elif _uniform(layers):
             first = layers[0]
-            _ops.commit_round([l.key_pool for l in layers], [l.value_pool for l in layers], first.batch_size,
-                              first.length, chosen, past, packet, **pos)
+            launches = [_ops.commit_round([l.key_pool for l in layers], [l.value_pool for l in layers],
+                                          first.batch_size, first.length, chosen, past, packet, **pos, launch=False)]
         else:
-            for i, layer in enumerate(layers):
-                _ops.commit_round([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length, chosen,
-                                  past, packet, **(pos if i == 0 else {}))
+            launches = [_ops.commit_round([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length,
+                                          chosen, past, packet, **(pos if i == 0 else {}), launch=False)
+                        for i, layer in enumerate(layers)]
+
+        def launch():
+            for go in launches:
+                go()
+
+        return launch if deferred else launch()
 
     def statistics(self):
         totals = {name: sum(layer.stats[name] for layer in self.layers) for name in LAYER_COUNTERS}

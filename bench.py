@@ -282,10 +282,11 @@ def verify_round(st, i, marks=None):
         if marks is not None:
             marks[k].record()
 
+    append = st.cache.update_layers(st.keys, st.values, deferred=True)  # host work ahead of the launches
     mark(0)
     vis = st.tree.visibility(st.past, st.pad, workspace=st.vis_ws)
     mark(1)
-    views = st.cache.update_layers(st.keys, st.values)
+    views = append()
     mark(2)
     for l in range(st.wl.layers):
         _ops.tree_attention_bits(st.queries[l], views[l][0], views[l][1], vis.bits, vis.first_col, st.scale,

@@ -174,5 +174,27 @@ def batched_layers_equal_per_layer(device):
     assert c.kv_rows_moved == 4 and c[2][0].shape[0] == 2
 
 
+def deferred_update_layers(device):
+    """update_layers(deferred=True) writes nothing and keeps the length until the returned
+    callable runs, then equals the immediate form."""
+    rng = np.random.RandomState(6)
+    layers, b, h, d = 2, 3, 2, 4
+    prefix = [rng.randn(b, h, 7, d).astype(np.float32) for _ in range(layers)]
+    tree = [rng.randn(b, h, 4, d).astype(np.float32) for _ in range(layers)]
+    c = OPDStaticCache(16, batch_capacity=b)
+    for l in range(layers):
+        c.update(to(device, prefix[l]), to(device, prefix[l] * 2), l)
+    launch = c.update_layers([to(device, x) for x in tree], [to(device, x * 2) for x in tree], deferred=True)
+    assert c.get_seq_length() == 7  # pools may have grown, but no row is written yet
+    before = [l.key_pool.clone() for l in c.layers]
+    views = launch()
+    assert all(not torch.equal(p[:, :, 7:11], l.key_pool[:, :, 7:11]) for p, l in zip(before, c.layers))
+    assert c.get_seq_length() == 11
+    for l in range(layers):
+        assert torch.equal(views[l][0], to(device, np.concatenate([prefix[l], tree[l]], 2)))
+        assert torch.equal(views[l][1], to(device, np.concatenate([prefix[l], tree[l]], 2) * 2))
+
+
 SCENARIOS_WITH_GOLDEN = (growth_repeat_select_crop, swap_remove_counters, persistent_pools, append_crop_repeat_select)
-SCENARIOS = (pools_freed_without_cycle, reference_error_messages, batched_layers_equal_per_layer)
+SCENARIOS = (pools_freed_without_cycle, reference_error_messages, batched_layers_equal_per_layer,
+             deferred_update_layers)

@@ -18,9 +18,14 @@ def _np(t):
     return t.numpy()
 
 
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length):
-    for kp, vp, ks, vs in zip(key_pools, value_pools, key_srcs, value_srcs):
-        oracle.append(_np(kp), _np(vp), _np(ks), _np(vs), length)
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True):
+    def go():
+        for kp, vp, ks, vs in zip(key_pools, value_pools, key_srcs, value_srcs):
+            oracle.append(_np(kp), _np(vp), _np(ks), _np(vs), length)
+    if launch:
+        go()
+        return None
+    return go
 
 
 def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width):
