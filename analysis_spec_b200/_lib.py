@@ -46,8 +46,12 @@ SIGNATURES = {
     'speckv_tree_attention': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                               ctypes.c_float, _i32, _p],
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],
+    'speckv_plan_launch': [_p, _p],
     'speckv_version': [],
 }
+
+# entries with a prepare / launch split (speckv_<name>_prepare + speckv_plan_launch)
+PREPARED = ('speckv_append_rows', 'speckv_commit_round')
 
 _lock = threading.Lock()
 _lib = None
@@ -72,6 +76,12 @@ def load():
             lib.speckv_last_error.restype = ctypes.c_char_p
             lib.speckv_remap_scratch_bytes.argtypes = [_i64, _i64, _i64, _i64, _i32]
             lib.speckv_remap_scratch_bytes.restype = ctypes.c_int64
+            for name in PREPARED:  # same arguments without the stream, then the plan out-pointer
+                fn = getattr(lib, name + '_prepare')
+                fn.argtypes = SIGNATURES[name][:-1] + [_pp]
+                fn.restype = ctypes.c_int
+            lib.speckv_plan_release.argtypes = [_p]
+            lib.speckv_plan_release.restype = None
             _lib = lib
     return _lib
 
@@ -115,6 +125,45 @@ def call(name, *args):
     profile.calls += 1
     if status != SPECKV_OK:
         raise SpecKVError(name, status, lib.speckv_last_error().decode(errors='replace'))
+
+
+class Plan:
+    """A prepared launch of entry point `name` (see speckv_plan_launch); freed with the object."""
+
+    def __init__(self, name, handle, stream):
+        self.name, self.handle, self.stream = name, handle, stream
+
+    def __call__(self):
+        """Enqueues the prepared kernel (profiled under the entry point's own name)."""
+        lib = load()
+        if profile.enabled:
+            import torch
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            status = lib.speckv_plan_launch(self.handle, self.stream)
+            end.record()
+            profile.events.setdefault(self.name, []).append((start, end))
+        else:
+            status = lib.speckv_plan_launch(self.handle, self.stream)
+        profile.calls += 1
+        if status != SPECKV_OK:
+            raise SpecKVError(self.name, status, lib.speckv_last_error().decode(errors='replace'))
+
+    def __del__(self):
+        if self.handle and _lib is not None:
+            _lib.speckv_plan_release(self.handle)
+            self.handle = None
+
+
+def prepare(name, *args):
+    """speckv_<name>_prepare with the entry point's arguments (the last one, the stream,
+    is kept for the launch); returns a Plan."""
+    lib = load()
+    handle = ctypes.c_void_p()
+    status = getattr(lib, name + '_prepare')(*args[:-1], ctypes.byref(handle))
+    if status != SPECKV_OK:
+        raise SpecKVError(name + '_prepare', status, lib.speckv_last_error().decode(errors='replace'))
+    return Plan(name, handle, args[-1])
 
 
 def ptr_array(values):

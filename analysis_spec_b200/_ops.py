@@ -73,13 +73,18 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=Tru
 
 
 def _issue(name, calls, launch):
-    """Issues prepared entry-point calls now, or returns a callable that issues them."""
-    def go():
+    """Issues the entry-point calls now, or prepares them (speckv_<name>_prepare: all
+    host-side checks and packing done here) and returns a callable whose only host
+    work is one kernel launch per call."""
+    if launch:
         for args in calls:
             _lib.call(name, *args)
-    if launch:
-        go()
         return None
+    plans = [_lib.prepare(name, *args) for args in calls]
+
+    def go():
+        for plan in plans:
+            plan()
     return go
 
 

@@ -440,6 +440,64 @@ int pool_vec(void* const* kp, void* const* vp, int layers, long long row_bytes) 
   return pick_vec(vals, n);
 }
 
+// A validated, packed launch: host work before the enqueue is done once, at preparation.
+struct LaunchPlan {
+  virtual ~LaunchPlan() = default;
+  virtual int launch(cudaStream_t s) const = 0;
+};
+struct EmptyPlan final : LaunchPlan {
+  int launch(cudaStream_t) const override { return SPECKV_OK; }
+};
+struct AppendPlan final : LaunchPlan {
+  PoolTable dst;
+  SrcTable src;
+  AppendGeom g;
+  int vec;
+  dim3 grid;
+  int launch(cudaStream_t s) const override {
+    constexpr int UNROLL = 4;
+    SPECKV_DISPATCH_VEC(vec, append_kernel<V, UNROLL><<<grid, kThreads, 0, s>>>(dst, src, g));
+    return check_launch("speckv_append_rows");
+  }
+};
+struct CommitPlan final : LaunchPlan {
+  PoolTable pools;
+  RoundGeom g;
+  unsigned long long* err;
+  int vec, maxr;
+  unsigned grid;
+  int launch(cudaStream_t s) const override {
+    if (maxr == 4) {
+      SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 4><<<grid, kThreads, 0, s>>>(pools, g, err));
+    } else if (maxr == 8) {
+      SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 8><<<grid, kThreads, 0, s>>>(pools, g, err));
+    } else {
+      SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 16><<<grid, kThreads, 0, s>>>(pools, g, err));
+    }
+    return check_launch("speckv_commit_round");
+  }
+};
+
+int prepare_append(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
+                   const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                   int64_t dim, int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                   const int64_t* value_src_strides, int32_t elem_bytes, LaunchPlan** out);
+int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t layers, int64_t batch, int64_t heads,
+                   int64_t dim, int64_t capacity, int64_t length, int32_t elem_bytes, const int64_t* chosen,
+                   int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, const int64_t* packet,
+                   int64_t packet_stride, int64_t max_width, uint8_t* pad_rows, int64_t pad_rows_stride,
+                   int64_t pad_rows_count, const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
+                   const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
+                   int64_t positions_stride_b, int64_t* past_positions, LaunchPlan** out);
+
+// Runs a prepared plan once and frees it.
+int launch_once(int st, LaunchPlan* plan, void* stream) {
+  if (st) return st;
+  const int r = plan->launch(static_cast<cudaStream_t>(stream));
+  delete plan;
+  return r;
+}
+
 }  // namespace
 }  // namespace speckv
 
@@ -451,6 +509,40 @@ extern "C" int speckv_append_rows(void* const* key_pools, void* const* value_poo
                                   int64_t dim, int64_t capacity, int64_t length,
                                   const int64_t* key_src_strides, const int64_t* value_src_strides,
                                   int32_t elem_bytes, void* stream) {
+  LaunchPlan* plan = nullptr;
+  const int st = prepare_append(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
+                                capacity, length, key_src_strides, value_src_strides, elem_bytes, &plan);
+  return launch_once(st, plan, stream);
+}
+
+extern "C" int speckv_append_rows_prepare(void* const* key_pools, void* const* value_pools,
+                                          const void* const* key_srcs, const void* const* value_srcs,
+                                          int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                                          int64_t dim, int64_t capacity, int64_t length,
+                                          const int64_t* key_src_strides, const int64_t* value_src_strides,
+                                          int32_t elem_bytes, void** plan) {
+  if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_append_rows_prepare: null plan");
+  LaunchPlan* p = nullptr;
+  const int st = prepare_append(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
+                                capacity, length, key_src_strides, value_src_strides, elem_bytes, &p);
+  *plan = st ? nullptr : p;
+  return st;
+}
+
+extern "C" int speckv_plan_launch(const void* plan, void* stream) {
+  if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_plan_launch: null plan");
+  return static_cast<const LaunchPlan*>(plan)->launch(static_cast<cudaStream_t>(stream));
+}
+
+extern "C" void speckv_plan_release(void* plan) { delete static_cast<LaunchPlan*>(plan); }
+
+namespace speckv {
+namespace {
+int prepare_append(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
+                           const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads,
+                           int64_t rows, int64_t dim, int64_t capacity, int64_t length,
+                           const int64_t* key_src_strides, const int64_t* value_src_strides, int32_t elem_bytes,
+                           LaunchPlan** out) {
   const char* fn = "speckv_append_rows";
   int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
   if (st) return st;
@@ -460,7 +552,10 @@ extern "C" int speckv_append_rows(void* const* key_pools, void* const* value_poo
   if (length + rows > capacity)
     return fail(SPECKV_EINVAL, "%s: length %lld + rows %lld exceeds capacity %lld", fn, (long long)length,
                 (long long)rows, (long long)capacity);
-  if (batch == 0 || rows == 0) return SPECKV_OK;
+  if (batch == 0 || rows == 0) {
+    *out = new EmptyPlan();
+    return SPECKV_OK;
+  }
   const long long row_bytes = dim * elem_bytes;
   long long vals[4 * SPECKV_MAX_LAYERS + 8];
   int n = 0;
@@ -484,9 +579,10 @@ extern "C" int speckv_append_rows(void* const* key_pools, void* const* value_poo
   const long long nvec = row_bytes / vec;
   const long long total = batch * heads * rows * nvec;
   if (!fits_u31(total)) return fail(SPECKV_ENOSUPPORT, "%s: %lld vectors per tensor exceeds 2^31", fn, total);
-  PoolTable dst;
+  AppendPlan* plan = new AppendPlan();
+  PoolTable& dst = plan->dst;
   fill_pools(dst, key_pools, value_pools, layers);
-  AppendGeom g;
+  AppendGeom& g = plan->g;
   g.nvec = FastDiv((uint32_t)nvec);
   g.rows = FastDiv((uint32_t)rows);
   g.heads = FastDiv((uint32_t)heads);
@@ -502,11 +598,14 @@ extern "C" int speckv_append_rows(void* const* key_pools, void* const* value_poo
   }
   g.total = (uint32_t)total;
   constexpr int UNROLL = 4;
-  dim3 grid((unsigned)((total + kThreads * UNROLL - 1) / (kThreads * UNROLL)), 2 * layers);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  SPECKV_DISPATCH_VEC(vec, append_kernel<V, UNROLL><<<grid, kThreads, 0, s>>>(dst, src, g));
-  return check_launch(fn);
+  plan->src = src;
+  plan->vec = vec;
+  plan->grid = dim3((unsigned)((total + kThreads * UNROLL - 1) / (kThreads * UNROLL)), 2 * layers);
+  *out = plan;
+  return SPECKV_OK;
 }
+}  // namespace
+}  // namespace speckv
 
 extern "C" int speckv_compact_suffix(void* const* key_pools, void* const* value_pools, int32_t layers,
                                      int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
@@ -575,6 +674,43 @@ extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_po
                                    uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
                                    int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
                                    int64_t* past_positions, void* stream) {
+  LaunchPlan* plan = nullptr;
+  const int st = prepare_commit(key_pools, value_pools, layers, batch, heads, dim, capacity, length, elem_bytes,
+                                chosen, chosen_stride_b, chosen_stride_w, past, packet, packet_stride, max_width,
+                                pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
+                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, &plan);
+  return launch_once(st, plan, stream);
+}
+
+extern "C" int speckv_commit_round_prepare(void* const* key_pools, void* const* value_pools, int32_t layers,
+                                           int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
+                                           int64_t length, int32_t elem_bytes, const int64_t* chosen,
+                                           int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past,
+                                           const int64_t* packet, int64_t packet_stride, int64_t max_width,
+                                           uint8_t* pad_rows, int64_t pad_rows_stride, int64_t pad_rows_count,
+                                           const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
+                                           const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
+                                           int64_t positions_stride_b, int64_t* past_positions, void** plan) {
+  if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_commit_round_prepare: null plan");
+  LaunchPlan* p = nullptr;
+  const int st = prepare_commit(key_pools, value_pools, layers, batch, heads, dim, capacity, length, elem_bytes,
+                                chosen, chosen_stride_b, chosen_stride_w, past, packet, packet_stride, max_width,
+                                pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
+                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, &p);
+  *plan = st ? nullptr : p;
+  return st;
+}
+
+namespace speckv {
+namespace {
+int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t layers, int64_t batch,
+                           int64_t heads, int64_t dim, int64_t capacity, int64_t length, int32_t elem_bytes,
+                           const int64_t* chosen, int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past,
+                           const int64_t* packet, int64_t packet_stride, int64_t max_width, uint8_t* pad_rows,
+                           int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
+                           uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
+                           int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
+                           int64_t* past_positions, LaunchPlan** out) {
   const char* fn = "speckv_commit_round";
   if (layers != 0) {
     int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
@@ -584,7 +720,10 @@ extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_po
   if (layers != 0 && (past > length || length > capacity))
     return fail(SPECKV_EINVAL, "%s: past %lld / length %lld / capacity %lld inconsistent", fn, (long long)past,
                 (long long)length, (long long)capacity);
-  if (batch == 0 || (layers == 0 && positions == nullptr)) return SPECKV_OK;
+  if (batch == 0 || (layers == 0 && positions == nullptr)) {
+    *out = new EmptyPlan();
+    return SPECKV_OK;
+  }
   if (packet == nullptr || packet_stride < 3) return fail(SPECKV_EINVAL, "%s: packet rows need 3 columns", fn);
   if (layers != 0 && chosen == nullptr) return fail(SPECKV_EINVAL, "%s: null chosen", fn);
   if (positions != nullptr) {
@@ -609,9 +748,10 @@ extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_po
     return fail(SPECKV_ENOSUPPORT, "%s: problem too large for 32-bit indexing", fn);
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
-  PoolTable pools;
+  CommitPlan* plan = new CommitPlan();
+  PoolTable& pools = plan->pools;
   if (layers != 0) fill_pools(pools, key_pools, value_pools, layers);
-  RoundGeom g;
+  RoundGeom& g = plan->g;
   g.c.bh = FastDiv((uint32_t)(batch * (layers != 0 ? heads : 1)));
   g.c.heads = FastDiv((uint32_t)(layers != 0 ? heads : 1));
   g.c.nvec = FastDiv((uint32_t)nvec);
@@ -633,19 +773,17 @@ extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_po
   g.compact_blocks = (uint32_t)compact_blocks;
   g.pos = PositionArgs{pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
                        newly_padded, np_stride_b, positions, positions_stride_b, past_positions};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned grid = (unsigned)(compact_blocks + position_blocks);
+  plan->err = err;
+  plan->vec = vec;
+  plan->grid = (unsigned)(compact_blocks + position_blocks);
   // register stage sized to the widest round the schedule allows (fewer registers, more resident warps)
   const long long stage = max_width * nvec;
-  if (stage <= 32 * 4) {
-    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 4><<<grid, kThreads, 0, s>>>(pools, g, err));
-  } else if (stage <= 32 * 8) {
-    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, 8><<<grid, kThreads, 0, s>>>(pools, g, err));
-  } else {
-    SPECKV_DISPATCH_VEC(vec, commit_round_kernel<V, MAXR><<<grid, kThreads, 0, s>>>(pools, g, err));
-  }
-  return check_launch(fn);
+  plan->maxr = stage <= 32 * 4 ? 4 : (stage <= 32 * 8 ? 8 : MAXR);
+  *out = plan;
+  return SPECKV_OK;
 }
+}  // namespace
+}  // namespace speckv
 
 // A CTA stages every batch row of up to kStageBytes / (rows * row bytes)
 // positions; a single position of all rows may take up to 3 * kStageBytes.

@@ -120,6 +120,34 @@ int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_
                         int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
                         int64_t* past_positions, void* stream);
 
+/* ---- Prepared launches -------------------------------------------------- */
+
+/* speckv_append_rows / speckv_commit_round split in two: *_prepare validates and
+ * packs the same arguments (without the stream) into *plan and launches nothing;
+ * speckv_plan_launch enqueues the prepared kernel on `stream`, whose host cost
+ * is then one kernel launch, so a caller can do the preparation while the GPU
+ * still runs the previous kernel. A plan keeps device pointers and sizes only
+ * (the caller keeps the buffers alive and unchanged in shape); it can be
+ * launched any number of times and is freed by speckv_plan_release. On error
+ * *plan is NULL. Same results as the one-call entries. */
+int speckv_append_rows_prepare(void* const* key_pools, void* const* value_pools,
+                               const void* const* key_srcs, const void* const* value_srcs,
+                               int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                               int64_t dim, int64_t capacity, int64_t length,
+                               const int64_t* key_src_strides, const int64_t* value_src_strides,
+                               int32_t elem_bytes, void** plan);
+int speckv_commit_round_prepare(void* const* key_pools, void* const* value_pools, int32_t layers,
+                                int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
+                                int64_t length, int32_t elem_bytes, const int64_t* chosen,
+                                int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past,
+                                const int64_t* packet, int64_t packet_stride, int64_t max_width,
+                                uint8_t* pad_rows, int64_t pad_rows_stride, int64_t pad_rows_count,
+                                const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
+                                const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
+                                int64_t positions_stride_b, int64_t* past_positions, void** plan);
+int speckv_plan_launch(const void* plan, void* stream);
+void speckv_plan_release(void* plan);
+
 /* ---- KV rows: batch remap (repeat / select) ---------------------------- */
 
 /* Row remap over the live prefix [0, length) of every layer:

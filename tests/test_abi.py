@@ -30,9 +30,11 @@ def lib():
 def test_every_declared_symbol_is_exported(lib):
     names = declared()
     assert len(names) >= 15
+    bound_elsewhere = {'speckv_last_error', 'speckv_remap_scratch_bytes', 'speckv_plan_release'}
+    bound_elsewhere |= {name + '_prepare' for name in _lib.PREPARED}
     for name in names:
         assert hasattr(lib, name), name
-        if name not in ('speckv_last_error', 'speckv_remap_scratch_bytes'):
+        if name not in bound_elsewhere:
             assert name in _lib.SIGNATURES, f'{name} has no ctypes signature'
 
 
@@ -57,3 +59,19 @@ def test_argument_errors_are_reported_without_a_launch(lib):
     with pytest.raises(_lib.SpecKVError, match='not a multiple'):
         _lib.call('speckv_tree_attention', None, strides, None, strides, None, strides, None, 0, None, 1, 3, 2, 1, 1,
                   8, 1.0, 1, None)
+
+
+def test_prepared_launch_host_side(lib):
+    """Preparation validates like the one-call entry (no launch on error); an empty
+    append prepares a plan whose launch does nothing, so it runs without a GPU."""
+    nul = (ctypes.c_void_p * 1)(None)
+    strides = _lib.i64_array([0, 0, 0])
+    with pytest.raises(_lib.SpecKVError, match='layers=0'):
+        _lib.prepare('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None)
+    pools = (ctypes.c_void_p * 1)(16)  # never dereferenced: batch 0 moves nothing
+    plan = _lib.prepare('speckv_append_rows', pools, pools, pools, pools, 1, 0, 1, 1, 8, 8, 0, strides, strides, 2,
+                        None)
+    assert plan.handle
+    plan()
+    plan()  # a plan can be launched again
+    del plan
