@@ -415,3 +415,36 @@ def device_error(device=None):
     if value >> 47:
         value -= 1 << 48
     return _lib.DEVICE_ERROR_KINDS.get(kind, str(kind)), value
+
+
+def _mask_operands(fn, mask, pad):
+    if not mask.is_contiguous() or mask.dim() != 4 or mask.shape[1] != 1:
+        raise ValueError(f'{fn}: mask must be a contiguous (batch, 1, query, columns) tensor')
+    if mask.dtype not in _DTYPE_CODE:
+        raise ValueError(f'{fn}: unsupported mask dtype {mask.dtype}')
+    if pad is None:
+        return 0, 0
+    if pad.dtype != torch.bool or pad.dim() != 2 or pad.shape[0] < mask.shape[0] or pad.shape[1] < mask.shape[3]:
+        raise ValueError(f'{fn}: padding must be a bool (batch, >= columns) tensor')
+    return pad.stride(0), pad.stride(1)
+
+
+def causal_mask(mask, past, pad=None):
+    """mask[b, 0, r, c] = 0 if c <= past + r and not pad[b, c] else finfo(dtype).min (one launch)."""
+    _require_cuda(mask, pad)
+    ps0, ps1 = _mask_operands('causal_mask', mask, pad)
+    batch, _, query, columns = mask.shape
+    _lib.call('speckv_causal_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, int(past), columns,
+              _ptr(pad), ps0, ps1, _stream(mask))
+
+
+def expansion_mask(mask, init_length, seen, pad=None):
+    """mask[b, 0, r, c] = 0 if (c < init_length or c == seen[b, r, 0]) and not pad[b, c], else
+    finfo(dtype).min; `seen` (batch, query[, 1]) int64 (one launch)."""
+    _require_cuda(mask, seen, pad)
+    ps0, ps1 = _mask_operands('expansion_mask', mask, pad)
+    batch, _, query, columns = mask.shape
+    if seen.dtype != torch.long or seen.shape[0] < batch or seen.shape[1] < query:
+        raise ValueError('expansion_mask: seen must be an int64 (batch, query[, 1]) tensor')
+    _lib.call('speckv_expansion_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, columns,
+              int(init_length), seen.data_ptr(), seen.stride(0), seen.stride(1), _ptr(pad), ps0, ps1, _stream(mask))

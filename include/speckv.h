@@ -44,6 +44,7 @@ extern "C" {
 #define SPECKV_DERR_OWNER_INDEX 5
 #define SPECKV_DERR_TIMEOUT 6  /* a bounded wait inside a kernel expired; value = wait site */
 #define SPECKV_DERR_PACKET 7   /* scheduling packet inconsistent with the commit; value = its width */
+#define SPECKV_DERR_SEEN_INDEX 8 /* draft expansion: seen position outside [0, columns) */
 
 /* dtype codes for masks / attention operands */
 #define SPECKV_F32 0
@@ -119,6 +120,30 @@ int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_
                         uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
                         int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
                         int64_t* past_positions, void* stream);
+
+/* ---- Draft-model attention masks ---------------------------------------- */
+
+/* Causal additive mask (batch, 1, query, columns), contiguous: entry (b, r, c) is 0
+ * when c <= past + r and pad[b][c] is false (pad may be NULL; element strides
+ * pad_stride_b, pad_stride_c), else the dtype's lowest finite value (dtype
+ * SPECKV_F32 / BF16 / F16). Replaces AttentionWorkspace.causal's CUDA branch
+ * (helper/opd_attention.py:31-43) and its kernel
+ * (helper/opd_attention_kernels.py:7-22). */
+int speckv_causal_mask(void* mask, int32_t dtype, int64_t batch, int64_t query, int64_t past,
+                       int64_t columns, const uint8_t* pad, int64_t pad_stride_b, int64_t pad_stride_c,
+                       void* stream);
+
+/* Draft expansion mask (batch, 1, query, columns), contiguous: entry (b, r, c) is 0
+ * when (c < init_length or c == seen[b][r]) and pad[b][c] is false, else the dtype's
+ * lowest value; seen is int64 with element strides (seen_stride_b, seen_stride_r).
+ * One launch for the zero / [init:] fill / scatter / padding fill sequence of
+ * helper/opd_generate.py:143-161 (bool padding form). A seen position outside
+ * [0, columns) sets device error SPECKV_DERR_SEEN_INDEX and that row sees only
+ * its first init_length columns. */
+int speckv_expansion_mask(void* mask, int32_t dtype, int64_t batch, int64_t query, int64_t columns,
+                          int64_t init_length, const int64_t* seen, int64_t seen_stride_b,
+                          int64_t seen_stride_r, const uint8_t* pad, int64_t pad_stride_b,
+                          int64_t pad_stride_c, void* stream);
 
 /* ---- Prepared launches -------------------------------------------------- */
 

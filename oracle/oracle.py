@@ -23,6 +23,8 @@ Reference code followed (file:line within the reference project):
   swap_remove_plan     helper/opd_static_cache.py:247-254
   position_update      helper/opd_generate.py:556-558, 644-650
   attention            transformers integrations/sdpa_attention.py:40-104 (repeat_kv + SDPA)
+  causal_visible       helper/opd_attention.py:31-43, helper/opd_attention_kernels.py:7-22
+  expansion_visible    helper/opd_generate.py:143-162
 """
 import ctypes
 import os
@@ -296,3 +298,30 @@ def attention(q, k, v, mask, scale):
         p /= p.sum(axis=-1, keepdims=True)
         out[b] = np.matmul(p, vv).transpose(1, 0, 2)
     return out
+
+
+def causal_visible(batch, query, past, columns, pad=None):
+    """Visibility (batch, query, columns) of the draft causal mask: c <= past + r, not padding."""
+    vis = np.arange(columns)[None, None, :] <= past + np.arange(query)[None, :, None]
+    vis = np.broadcast_to(vis, (batch, query, columns)).copy()
+    if pad is not None:
+        vis &= ~np.asarray(pad, dtype=bool)[:, None, :columns]
+    return vis
+
+
+def expansion_visible(batch, query, columns, init_length, seen, pad=None, pad_pairs=None):
+    """Visibility (batch, query, columns) of a draft expansion step: columns below init_length
+    and the row's own column seen[b, r]; padding (bool (batch, >= columns) and / or (n, 2)
+    pairs (b, column)) off last."""
+    vis = np.zeros((batch, query, columns), dtype=bool)
+    vis[:, :, :init_length] = True
+    seen = np.asarray(seen, dtype=np.int64).reshape(batch, -1)[:, :query]
+    b_idx = np.arange(batch)[:, None].repeat(query, 1)
+    r_idx = np.arange(query)[None, :].repeat(batch, 0)
+    vis[b_idx, r_idx, seen] = True
+    if pad is not None:
+        vis &= ~np.asarray(pad, dtype=bool)[:, None, :columns]
+    if pad_pairs is not None:
+        for b, c in np.asarray(pad_pairs, dtype=np.int64).reshape(-1, 2):
+            vis[b, :, c] = False
+    return vis

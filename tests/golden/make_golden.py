@@ -339,6 +339,54 @@ def attention_cases():
     save('attention', count=len(specs), **out)
 
 
+def draft_mask_cases():
+    """Draft-model masks: AttentionWorkspace.causal on CPU (torch branch) and the Triton kernel
+    helper/opd_attention_kernels.causal_mask (interpreted on CPU tensors); the expansion mask
+    by the reference's op sequence helper/opd_generate.py:143-162 on CPU tensors."""
+    from helper.opd_attention import AttentionWorkspace
+    from helper.opd_attention_kernels import causal_mask
+    rng = np.random.RandomState(23)
+    out = {}
+    specs = [(3, 5, 17, torch.float32, True), (2, 10, 40, torch.bfloat16, False), (4, 1, 9, torch.float16, True),
+             (2, 7, 300, torch.bfloat16, True)]
+    for n, (batch, query, past, dtype, with_pad) in enumerate(specs):
+        cols = past + query
+        pad = torch.from_numpy(rng.rand(batch, cols + 3) < 0.2) if with_pad else None
+        ws = AttentionWorkspace('cpu')
+        ref = ws.causal('m', past, query, batch, dtype, pad).clone()
+        tri = torch.empty(batch, 1, query, cols, dtype=dtype)
+        causal_mask(tri, past, pad)
+        assert torch.equal(ref, tri), 'torch and Triton branches disagree'
+        out[f'c{n}_shape'] = np.array([batch, query, past])
+        out[f'c{n}_dtype'] = str(dtype).split('.')[-1]
+        out[f'c{n}_pad'] = pad.numpy() if pad is not None else np.zeros((0, 0), dtype=bool)
+        out[f'c{n}_visible'] = (ref.float() == 0).numpy()[:, 0]
+    especs = [(3, 4, 30, 12, torch.float32, 'bool'), (2, 10, 64, 20, torch.bfloat16, 'pairs'),
+              (4, 3, 12, 9, torch.float16, None), (2, 6, 200, 150, torch.bfloat16, 'bool')]
+    for n, (batch, k, cols, init, dtype, pad_kind) in enumerate(especs):
+        seen = torch.from_numpy(rng.randint(init, cols, size=(batch, k, 1)).astype(np.int64))
+        mask = torch.empty(batch, 1, k, cols, dtype=dtype)
+        lowest = torch.finfo(dtype).min
+        mask.zero_()
+        mask[..., init:] = lowest
+        mask.scatter_(dim=-1, index=seen.unsqueeze(1), value=0.)
+        pad = pairs = None
+        if pad_kind == 'bool':
+            pad = torch.from_numpy(rng.rand(batch, cols + 5) < 0.15)
+            mask.masked_fill_(pad[:, None, None, :mask.shape[-1]], lowest)
+        elif pad_kind == 'pairs':
+            pairs = torch.from_numpy(np.array([[b, c] for b in range(batch) for c in rng.choice(cols, 4, replace=False)],
+                                              dtype=np.int64))
+            mask[pairs[:, 0], 0, :, pairs[:, 1]] = lowest
+        out[f'e{n}_shape'] = np.array([batch, k, cols, init])
+        out[f'e{n}_dtype'] = str(dtype).split('.')[-1]
+        out[f'e{n}_seen'] = seen.numpy()
+        out[f'e{n}_pad'] = pad.numpy() if pad is not None else np.zeros((0, 0), dtype=bool)
+        out[f'e{n}_pairs'] = pairs.numpy() if pairs is not None else np.zeros((0, 2), dtype=np.int64)
+        out[f'e{n}_visible'] = (mask.float() == 0).numpy()[:, 0]
+    save('draft_masks', causal_count=len(specs), expansion_count=len(especs), **out)
+
+
 if __name__ == '__main__':
     torch.manual_seed(0)
     kv_sequence()
@@ -349,3 +397,4 @@ if __name__ == '__main__':
     schedule_kat()
     tree_cases()
     attention_cases()
+    draft_mask_cases()
