@@ -46,13 +46,29 @@ constexpr uint32_t STAGE_BYTES = 2 * kTileBytes;  // K + V
 constexpr uint32_t P_OFF = KV_OFF + kStages * STAGE_BYTES;
 constexpr uint32_t BAR_OFF = P_OFF + kTileBytes;
 constexpr uint32_t SMEM_BYTES = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+// Staged dense mask (MODE 2): warps 2-3 copy the mask rows of the CTA's 128 packed rows
+// (at most 127 / g + 2 tree rows) for each key tile into a 2-stage shared-memory ring, all
+// loads of a tile in flight at once; rows padded by 16 bytes so the softmax warps' row reads
+// fall in distinct banks. Query groups g >= 4 (16-bit masks) or g >= 5 (fp32 masks).
+constexpr uint32_t MASK_OFF = BAR_OFF + 256;
+template <typename MT>
+__host__ __device__ constexpr int mask_cta_rows() { return sizeof(MT) == 4 ? 27 : 33; }
+template <typename MT>
+__host__ __device__ constexpr int mask_min_group() { return sizeof(MT) == 4 ? 5 : 4; }
+template <typename MT>
+__host__ __device__ constexpr uint32_t mask_row_bytes() { return BN * (uint32_t)sizeof(MT) + 16u; }
+template <typename MT>
+__host__ __device__ constexpr uint32_t mask_stage_bytes() { return mask_cta_rows<MT>() * mask_row_bytes<MT>(); }
+static_assert(127 / 4 + 2 <= 33 && 127 / 5 + 2 <= 27, "a CTA's tree rows must fit its mask stage");
+static_assert(SMEM_BYTES + 2 * mask_stage_bytes<float>() <= 232448 &&
+              SMEM_BYTES + 2 * mask_stage_bytes<uint16_t>() <= 232448, "staged mask exceeds shared memory");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t S_COL0 = 0, O_COL = 256;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
 // barrier slots (8 bytes each) after BAR_OFF
 enum { B_KV_FULL = 0, B_KV_EMPTY = 2, B_S_FULL = 4, B_S_FREE = 6, B_P_FULL = 8, B_O_DONE = 9, B_Q_READY = 10,
-       B_DRAIN = 11, B_ABORT = 12, TMEM_SLOT = 13 };
+       B_DRAIN = 11, B_ABORT = 12, TMEM_SLOT = 13, B_M_FULL = 14, B_M_EMPTY = 16 };
 
 struct Sm100Args {
   const void* q;
@@ -259,10 +275,25 @@ __device__ __forceinline__ float mask_value<__half>(const void* mask, long long 
   return __half2float(static_cast<const __half*>(mask)[idx]);
 }
 
+// raw bits of one mask element and their float value
+template <typename MT> struct MaskRaw { using type = uint16_t; };
+template <> struct MaskRaw<float> { using type = uint32_t; };
+template <typename MT>
+__device__ __forceinline__ float mask_raw_value(uint32_t raw);
+template <>
+__device__ __forceinline__ float mask_raw_value<float>(uint32_t raw) { return __uint_as_float(raw); }
+template <>
+__device__ __forceinline__ float mask_raw_value<__nv_bfloat16>(uint32_t raw) { return __uint_as_float(raw << 16); }
+template <>
+__device__ __forceinline__ float mask_raw_value<__half>(uint32_t raw) {
+  return __half2float(__ushort_as_half((unsigned short)raw));
+}
+
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
-// MODE 0: visibility bits; MODE 1: dense additive mask of type MT.
+// MODE 0: visibility bits; MODE 1: dense additive mask of type MT read per thread from
+// global memory; MODE 2: the same mask staged in shared memory by warps 2-3.
 template <typename T, int MODE, typename MT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_sm100_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -294,6 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_KV_EMPTY + i), 1);
       mbar_init(bar(B_S_FULL + i), 1);
       mbar_init(bar(B_S_FREE + i), 128);
+      mbar_init(bar(B_M_FULL + i), 64);
+      mbar_init(bar(B_M_EMPTY + i), 128);
     }
     mbar_init(bar(B_P_FULL), 128);
     mbar_init(bar(B_O_DONE), 1);
@@ -380,6 +413,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(bar(B_DRAIN));
       drain_wait(bar(B_DRAIN), 0);
     }
+  } else if (MODE == 2 && warp < 4) {
+    // ---------------- mask loader (warps 2-3) ----------------
+    using Raw = typename MaskRaw<MT>::type;
+    constexpr int kLoads = 2 * mask_cta_rows<MT>();  // per thread: 64 threads x kLoads >= rows x 128
+    const int lt = threadIdx.x - 64;
+    const int r_lo = (mt * BM) / a.group;
+    const int nr = (min(total_rows, mt * BM + BM) - 1) / a.group - r_lo + 1;
+    const Raw* src = static_cast<const Raw*>(a.mask) + ((long long)b * a.rows + r_lo) * a.kv_len;
+    for (int it = 0; it < n_tiles; ++it) {
+      const int s = it & 1;
+      if (it >= 2 && !mbar_wait(bar(B_M_EMPTY + s), ((it >> 1) - 1) & 1, abort_flag, a.err, 11)) break;
+      const int c0 = (tile0 + it) * BN;
+      // element u of this thread: row u / 2, column (u % 2) * 64 + lt of the tile
+      Raw v[kLoads];
+#pragma unroll
+      for (int u = 0; u < kLoads; ++u) {
+        const int rr = u >> 1, c = (u & 1) * 64 + lt;
+        v[u] = (rr < nr && c0 + c < a.kv_len) ? __ldg(src + (long long)rr * a.kv_len + c0 + c) : Raw(0);
+      }
+      uint8_t* dst = smem + MASK_OFF + s * mask_stage_bytes<MT>();
+#pragma unroll
+      for (int u = 0; u < kLoads; ++u) {
+        const int rr = u >> 1, c = (u & 1) * 64 + lt;
+        if (rr < nr) *reinterpret_cast<Raw*>(dst + rr * mask_row_bytes<MT>() + c * sizeof(Raw)) = v[u];
+      }
+      mbar_arrive(bar(B_M_FULL + s));
+    }
   } else if (warp >= 4) {
     // ---------------- softmax warpgroup ----------------
     const int t = threadIdx.x - 128;  // row within the tile == TMEM lane
@@ -400,6 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();
       mbar_arrive(bar(B_Q_READY));
     }
+    using Raw = typename MaskRaw<MT>::type;
+    const int r_lo = (mt * BM) / a.group;  // MODE 2: first tree row of the staged mask rows
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int it = 0; it < n_tiles; ++it) {
@@ -425,6 +487,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           x[i] = vis ? x[i] * a.scale_log2 : -INFINITY;
           mx = fmaxf(mx, x[i]);
         }
+      } else if (MODE == 2) {
+        ok = mbar_wait(bar(B_M_FULL + s), (it >> 1) & 1, abort_flag, a.err, 10);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const uint8_t* mrow = smem + MASK_OFF + s * mask_stage_bytes<MT>() + (valid ? r - r_lo : 0) * mask_row_bytes<MT>();
+        constexpr float kLog2e = 1.4426950408889634f;
+        constexpr int kPer = 16 / (int)sizeof(Raw);
+#pragma unroll
+        for (int i0 = 0; i0 < BN; i0 += kPer) {
+          const uint4 w = *reinterpret_cast<const uint4*>(mrow + i0 * sizeof(Raw));
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int j = 0; j < kPer; ++j) {
+            const uint32_t raw = sizeof(Raw) == 4 ? wv[j] : (wv[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu;
+            const int i = i0 + j;
+            x[i] = col0 + i < a.kv_len ? x[i] * a.scale_log2 + mask_raw_value<MT>(raw) * kLog2e : -INFINITY;
+            mx = fmaxf(mx, x[i]);
+          }
+          // at most four 16-byte reads in flight: keeps fp32 masks within the register budget
+          if (sizeof(Raw) == 4 && (i0 / kPer) % 4 == 3) asm volatile("" ::: "memory");
+        }
+        mbar_arrive(bar(B_M_EMPTY + s));  // stage s may take the rows of tile it + 2
       } else {
         const long long mrow = ((long long)b * a.rows + r) * a.kv_len;
         constexpr float kLog2e = 1.4426950408889634f;
@@ -1079,9 +1162,10 @@ bool make_kv_map(CUtensorMap* map, const void* base, const long long* st, long l
 template <typename T, int MODE, typename MT>
 int launch_sm100(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, cudaStream_t stream) {
   auto kern = attn_sm100_kernel<T, MODE, MT>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+  const uint32_t smem = SMEM_BYTES + (MODE == 2 ? 2 * mask_stage_bytes<MT>() : 0u);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const long long grid = (long long)s.batch * s.kv_heads * s.mtiles;
-  kern<<<(unsigned)grid, kThreads, SMEM_BYTES, stream>>>(mk, mv, s);
+  kern<<<(unsigned)grid, kThreads, smem, stream>>>(mk, mv, s);
   return check_launch("speckv_tree_attention(sm100)");
 }
 
@@ -1159,6 +1243,20 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
     return bf ? launch_pair<__nv_bfloat16>(mk, mv, s, stream) : launch_pair<__half>(mk, mv, s, stream);
+  }
+  const int min_group = a.mask_dtype == SPECKV_F32 ? mask_min_group<float>() : mask_min_group<uint16_t>();
+  if (a.mask != nullptr && s.group >= min_group) {
+    switch (a.mask_dtype) {
+      case SPECKV_BF16:
+        return bf ? launch_sm100<__nv_bfloat16, 2, __nv_bfloat16>(mk, mv, s, stream)
+                  : launch_sm100<__half, 2, __nv_bfloat16>(mk, mv, s, stream);
+      case SPECKV_F16:
+        return bf ? launch_sm100<__nv_bfloat16, 2, __half>(mk, mv, s, stream)
+                  : launch_sm100<__half, 2, __half>(mk, mv, s, stream);
+      default:
+        return bf ? launch_sm100<__nv_bfloat16, 2, float>(mk, mv, s, stream)
+                  : launch_sm100<__half, 2, float>(mk, mv, s, stream);
+    }
   }
   switch (a.mask == nullptr ? SPECKV_F32 : a.mask_dtype) {
     case SPECKV_BF16:

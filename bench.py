@@ -19,6 +19,8 @@ Reported (one JSON line on rank 0):
              inputs copied from pinned host memory and the packet read back
   roofline   the append kernel (dominant commit kernel) vs measured HBM copy peak
   cpu_baseline  the CPU oracle on a bounded sample of the same work
+  draft_step   one draft expansion step (mask + attention of one draft layer),
+             this library's launches beside the reference's torch sequence
 
 ``--impl reference`` times the CPU restatement of the reference's path (the
 reference is Python/torch and cannot run on the GPU host) on the host cores.
@@ -374,6 +376,7 @@ def run_ours(args):
     job_commit_bytes = moved.item()
 
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
+    draft = measure_draft(st) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
     append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
     append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
@@ -406,6 +409,7 @@ def run_ours(args):
         'acceptance': totals,
         'clocks': clock,
         'e2e': e2e,
+        'draft_step': draft,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(wl, budget_s=12.0)
@@ -413,6 +417,74 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def measure_draft(st, iters=20, warmup=3):
+    """One draft expansion step of one draft layer at the workload's batch, heads and shared
+    past (draft K = the tree's top-k): the expansion mask and the draft attention, each as
+    this library's launch and as the reference's torch sequence on the same GPU (zero /
+    [init:] fill / scatter / padding fill, helper/opd_generate.py:143-162; repeat_kv + SDPA,
+    helper/fastgrpo_model.py:58-69). Device time per step from CUDA events around `iters`
+    back-to-back steps; the K/V views (> L2) are strided cache views."""
+    import torch
+    import torch.nn.functional as F
+    from analysis_spec_b200.draft_attention import draft_sdpa
+    from analysis_spec_b200.opd_attention import expansion_mask
+    wl, dev, dtype = st.wl, st.device, st.dtype
+    B, Hkv, Hq, D, k = wl.batch, wl.kv_heads, wl.q_heads, wl.dim, wl.topk
+    past = st.past
+    cols = past + k
+    init = past - 2 * k
+    gen = torch.Generator(device=dev).manual_seed(11)
+    pool_k = torch.randn(B, Hkv, cols + 256, D, device=dev, generator=gen).to(dtype)
+    pool_v = torch.randn(B, Hkv, cols + 256, D, device=dev, generator=gen).to(dtype)
+    keys, values = pool_k[:, :, :cols], pool_v[:, :, :cols]
+    q = torch.randn(B, Hq, k, D, device=dev, generator=gen).to(dtype)
+    seen = torch.randint(init, cols, (B, k, 1), device=dev, generator=gen)
+    pad = st.pad
+    mask = torch.empty(B, 1, k, cols, device=dev, dtype=dtype)
+    lowest = torch.finfo(dtype).min
+    g = Hq // Hkv
+
+    def ours_mask():
+        expansion_mask(mask, init, seen, pad)
+
+    def torch_mask():
+        mask.zero_()
+        mask[..., init:] = lowest
+        mask.scatter_(dim=-1, index=seen.unsqueeze(1), value=0.)
+        mask.masked_fill_(pad[:, None, None, :cols], lowest)
+
+    def ours_attn():
+        draft_sdpa(q, keys, values, mask, g)
+
+    def torch_attn():
+        kk = keys[:, :, None].expand(B, Hkv, g, cols, D).reshape(B, Hq, cols, D)
+        vv = values[:, :, None].expand(B, Hkv, g, cols, D).reshape(B, Hq, cols, D)
+        F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / iters
+
+    torch_mask()
+    ref_mask = mask.clone()
+    ours_mask()
+    same = bool(torch.equal(mask.view(torch.int16), ref_mask.view(torch.int16)))
+    out = {'shape': f'batch {B}, draft_k {k}, columns {cols}, {Hq}q/{Hkv}kv x {D}, one draft layer',
+           'mask_us': round(timed(ours_mask), 2), 'mask_us_torch_sequence': round(timed(torch_mask), 2),
+           'attention_us': round(timed(ours_attn), 2), 'attention_us_torch_sdpa': round(timed(torch_attn), 2),
+           'mask_bit_exact_vs_torch_sequence': same}
+    del pool_k, pool_v
+    return out
 
 
 def measure_e2e(st, args, world):
