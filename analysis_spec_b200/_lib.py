@@ -15,7 +15,7 @@ F32, BF16, F16 = 0, 1, 2
 
 DEVICE_ERROR_KINDS = {1: 'remap index', 2: 'compact index', 3: 'move index', 4: 'tree parent index',
                       5: 'padding owner index', 6: 'wait timeout', 7: 'scheduling packet',
-                      8: 'seen index'}
+                      8: 'seen index', 9: 'history index'}
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -49,6 +49,9 @@ SIGNATURES = {
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],
     'speckv_plan_launch': [_p, _p],
     'speckv_causal_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p],
+    'speckv_history_append': [_i32, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pi64, _pi64, _pi64, _pi64,
+                              _p, _p, _i64, _i64, _p],
+    'speckv_history_pack': [_p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_expansion_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_version': [],
 }

@@ -448,3 +448,75 @@ def expansion_mask(mask, init_length, seen, pad=None):
         raise ValueError('expansion_mask: seen must be an int64 (batch, query[, 1]) tensor')
     _lib.call('speckv_expansion_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, columns,
               int(init_length), seen.data_ptr(), seen.stride(0), seen.stride(1), _ptr(pad), ps0, ps1, _stream(mask))
+
+
+def _position_layout(fn, t):
+    """(row stride, position stride) in bytes and bytes per position of a (rows, positions,
+    *element) tensor whose element dims are contiguous."""
+    es = t.element_size()
+    expect = 1
+    for size, stride in zip(reversed(t.shape[2:]), reversed(t.stride()[2:])):
+        if size != 1 and stride != expect:
+            raise ValueError(f'{fn}: element dims of a history tensor must be contiguous')
+        expect *= size
+    return t.stride(0) * es, t.stride(1) * es, expect * es
+
+
+def history_append(fields, owners, pool_rows, n, src_rows=None):
+    """One launch over up to four history fields. Each field is a tuple
+    (pool, src, index, gathered, start, width): pool (pool_rows, capacity, *elem) or None;
+    src (rows, positions, *elem); index int64 (n, width) source positions or None (w);
+    gathered contiguous (n, width, *elem) or None. owners int64 (n,) pool rows;
+    src_rows int64 (n,) source rows or None (i)."""
+    if not 1 <= len(fields) <= 4:
+        raise ValueError('history_append: 1..4 fields')
+    pools, pstr, srcs, sstr, idx, istr, gath, rbytes, spos, starts, widths, caps = ([] for _ in range(12))
+    for pool, src, index, gathered, start, width in fields:
+        _require_cuda(pool, src, index, gathered)
+        sr, sp, rb = _position_layout('history_append', src)
+        if pool is not None:
+            if pool.dtype != src.dtype or tuple(pool.shape[2:]) != tuple(src.shape[2:]):
+                raise ValueError('history_append: pool and source element shape / dtype differ')
+            pr, pp, _ = _position_layout('history_append', pool)
+        else:
+            pr = pp = 0
+        if index is not None and (index.dtype != torch.long or index.dim() != 2 or index.shape[0] < n or
+                                  index.shape[1] < width):
+            raise ValueError('history_append: index must be an int64 (n, width) tensor')
+        if gathered is not None and (not gathered.is_contiguous() or gathered.dtype != src.dtype or
+                                     gathered.numel() * gathered.element_size() < n * width * rb):
+            raise ValueError('history_append: gathered must be a contiguous (n, width, *element) tensor')
+        pools.append(_ptr(pool))
+        pstr += [pr, pp]
+        srcs.append(src.data_ptr())
+        sstr += [sr, sp]
+        idx.append(_ptr(index))
+        istr += list(index.stride()) if index is not None else [0, 0]
+        gath.append(_ptr(gathered))
+        rbytes.append(rb)
+        spos.append(src.shape[1])
+        starts.append(int(start))
+        widths.append(int(width))
+        caps.append(pool.shape[1] if pool is not None else 0)
+    _require_cuda(owners, src_rows)
+    for t in (owners, src_rows):
+        if t is not None and (t.dtype != torch.long or not t.is_contiguous() or t.numel() < n):
+            raise ValueError('history_append: owners / src_rows must be contiguous int64 with n entries')
+    ref = fields[0][1]
+    _lib.call('speckv_history_append', len(fields), _lib.ptr_array(pools), _lib.i64_array(pstr),
+              _lib.ptr_array(srcs), _lib.i64_array(sstr), _lib.ptr_array(idx), _lib.i64_array(istr),
+              _lib.ptr_array(gath), _lib.i64_array(rbytes), _lib.i64_array(spos), _lib.i64_array(starts),
+              _lib.i64_array(widths), _lib.i64_array(caps), _ptr(owners), _ptr(src_rows), int(n), int(pool_rows),
+              _stream(ref))
+
+
+def history_pack(dst, pool, offsets, rows, max_length):
+    """dst (total, *elem) contiguous <- the used prefix of each pool row; offsets int64 (rows + 1,)."""
+    _require_cuda(dst, pool, offsets)
+    pr, pp, rb = _position_layout('history_pack', pool)
+    if not dst.is_contiguous() or dst.dtype != pool.dtype:
+        raise ValueError('history_pack: dst must be contiguous with the pool dtype')
+    if offsets.dtype != torch.long or not offsets.is_contiguous() or offsets.numel() < rows + 1:
+        raise ValueError('history_pack: offsets must be contiguous int64 with rows + 1 entries')
+    _lib.call('speckv_history_pack', dst.data_ptr(), pool.data_ptr(), pr, pp, rb, offsets.data_ptr(), int(rows),
+              int(max_length), _stream(pool))

@@ -45,6 +45,9 @@ extern "C" {
 #define SPECKV_DERR_TIMEOUT 6  /* a bounded wait inside a kernel expired; value = wait site */
 #define SPECKV_DERR_PACKET 7   /* scheduling packet inconsistent with the commit; value = its width */
 #define SPECKV_DERR_SEEN_INDEX 8 /* draft expansion: seen position outside [0, columns) */
+#define SPECKV_DERR_HISTORY_INDEX 9 /* history append: owner row or source position out of range */
+
+#define SPECKV_HISTORY_MAX_FIELDS 4
 
 /* dtype codes for masks / attention operands */
 #define SPECKV_F32 0
@@ -144,6 +147,40 @@ int speckv_expansion_mask(void* mask, int32_t dtype, int64_t batch, int64_t quer
                           int64_t init_length, const int64_t* seen, int64_t seen_stride_b,
                           int64_t seen_stride_r, const uint8_t* pad, int64_t pad_stride_b,
                           int64_t pad_stride_c, void* stream);
+
+/* ---- Rollout history ---------------------------------------------------- */
+
+/* Appends positions to up to SPECKV_HISTORY_MAX_FIELDS history pools in one launch:
+ *   pool_f[owners[i]][starts[f] + w] = src_f[src_rows ? src_rows[i] : i][index_f ? index_f[i][w] : w]
+ * for i < n, w < widths[f]; with gathered[f] non-NULL the same elements also go
+ * to a contiguous (n, widths[f], row_bytes[f]) buffer, and with pools[f] NULL
+ * only there. Strides: pool_strides / src_strides are (row, position) pairs in
+ * BYTES per field; index_strides (row, position) pairs in elements; a position
+ * holds row_bytes[f] bytes (any element type). src_positions[f] bounds the
+ * source position; starts[f] + widths[f] must not exceed capacities[f]. An owner
+ * outside [0, pool_rows) or a source position outside [0, src_positions[f]) sets
+ * device error SPECKV_DERR_HISTORY_INDEX and that element is skipped.
+ * Replaces ContiguousRolloutHistory.append's per-field index_copy_
+ * (helper/opd_history.py:24-42), the initial repeated copy (:12-22) and the grow
+ * copy (:34-38); with an index it fuses the accepted-feature gather
+ * (helper/opd_generate.py:567-571) with the append of :572-579. */
+int speckv_history_append(int32_t fields, void* const* pools, const int64_t* pool_strides,
+                          const void* const* srcs, const int64_t* src_strides,
+                          const int64_t* const* indices, const int64_t* index_strides,
+                          void* const* gathered, const int64_t* row_bytes,
+                          const int64_t* src_positions, const int64_t* starts, const int64_t* widths,
+                          const int64_t* capacities, const int64_t* owners, const int64_t* src_rows,
+                          int64_t n, int64_t pool_rows, void* stream);
+
+/* Packs the used prefix of every pool row into dst (contiguous, row_bytes per
+ * position): dst[offsets[r] + p] = pool[r][p] for p < offsets[r + 1] - offsets[r],
+ * r < rows; offsets is a device array of rows + 1 int64 values, max_length the
+ * longest row (grid sizing only). Pool strides in bytes. Replaces the
+ * repeat_interleave + index_select gather of ContiguousRolloutHistory.finalize
+ * (helper/opd_history.py:52-67). */
+int speckv_history_pack(void* dst, const void* pool, int64_t pool_row_stride, int64_t pool_pos_stride,
+                        int64_t row_bytes, const int64_t* offsets, int64_t rows, int64_t max_length,
+                        void* stream);
 
 /* ---- Prepared launches -------------------------------------------------- */
 

@@ -25,6 +25,8 @@ Reference code followed (file:line within the reference project):
   attention            transformers integrations/sdpa_attention.py:40-104 (repeat_kv + SDPA)
   causal_visible       helper/opd_attention.py:31-43, helper/opd_attention_kernels.py:7-22
   expansion_visible    helper/opd_generate.py:143-162
+  RolloutHistory       helper/opd_history.py:10-67
+  gather_positions     helper/opd_generate.py:567-571 (accepted-feature gather)
 """
 import ctypes
 import os
@@ -325,3 +327,59 @@ def expansion_visible(batch, query, columns, init_length, seen, pad=None, pad_pa
         for b, c in np.asarray(pad_pairs, dtype=np.int64).reshape(-1, 2):
             vis[b, :, c] = False
     return vis
+
+
+# ---------------------------------------------------------------------------
+# rollout history
+# ---------------------------------------------------------------------------
+def gather_positions(tree, index):
+    """out[b, w] = tree[b, index[b, w]] for a (B, T, ...) array and (B, W) positions."""
+    tree = np.asarray(tree)
+    index = np.asarray(index, dtype=np.int64)
+    return tree[np.arange(tree.shape[0])[:, None], index]
+
+
+class RolloutHistory:
+    """Contiguous per-response pools: rows = batch x repeats, capacity max(length, max_length),
+    grown to max(end, 2 x capacity) on overflow; append writes chunk row i at the pool row
+    owners[i] from the field's current length; finalize returns each row's prefix of the
+    lengths recorded when the row finished (or at the end)."""
+
+    def __init__(self, initial, repeats, max_length):
+        sizes = {a.shape[0] for a in initial.values()}
+        assert len(sizes) == 1 and repeats >= 1 and max_length >= 1
+        self.rows = sizes.pop() * repeats
+        self.pools, self.lengths, self.capacities, self.finished = {}, {}, {}, {}
+        for name, a in initial.items():
+            a = np.asarray(a)
+            cap = max(a.shape[1], int(max_length))
+            pool = np.zeros((self.rows, cap) + a.shape[2:], dtype=a.dtype)
+            pool[:, :a.shape[1]] = np.repeat(a, repeats, axis=0)
+            self.pools[name], self.lengths[name], self.capacities[name] = pool, a.shape[1], cap
+
+    def append(self, owners, chunks):
+        owners = np.asarray(owners, dtype=np.int64)
+        for name, chunk in chunks.items():
+            chunk = np.asarray(chunk)
+            pool = self.pools[name]
+            start = self.lengths[name]
+            end = start + chunk.shape[1]
+            if end > pool.shape[1]:
+                cap = max(end, 2 * pool.shape[1])
+                grown = np.zeros((self.rows, cap) + pool.shape[2:], dtype=pool.dtype)
+                grown[:, :start] = pool[:, :start]
+                self.pools[name] = pool = grown
+                self.capacities[name] = cap
+            pool[owners, start:end] = chunk
+            self.lengths[name] = end
+
+    def mark_finished(self, row):
+        assert row not in self.finished
+        self.finished[row] = dict(self.lengths)
+
+    def finalize(self):
+        for row in range(self.rows):
+            if row not in self.finished:
+                self.mark_finished(row)
+        return [{name: pool[row, :self.finished[row][name]].copy() for name, pool in self.pools.items()}
+                for row in range(self.rows)]

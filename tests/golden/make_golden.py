@@ -387,6 +387,46 @@ def draft_mask_cases():
     save('draft_masks', causal_count=len(specs), expansion_count=len(especs), **out)
 
 
+def history_cases():
+    """ContiguousRolloutHistory (helper/opd_history.py:10-67) on CPU through a rollout:
+    repeated initial copy, three verify rounds whose chunks follow helper/opd_generate.py:567-579
+    (accepted features gathered from the tree hidden states at chosen_index - past, then appended
+    with generated_ids / input_ids to the owner rows), two capacity grows, rows finishing between
+    rounds, finalize."""
+    from helper.opd_history import ContiguousRolloutHistory
+    rng = np.random.RandomState(31)
+    batch, repeats, dim, tree_rows = 3, 2, 8, 10
+    init_len = 4
+    initial = {'generated_ids': torch.from_numpy(rng.randint(0, 1000, size=(batch, init_len))),
+               'features': torch.from_numpy(rng.randn(batch, init_len, dim).astype(np.float16)),
+               'input_ids': torch.from_numpy(rng.randint(0, 1000, size=(batch, init_len)))}
+    hist = ContiguousRolloutHistory(initial, repeats=repeats, max_length=6)
+    out = {f'init_{k}': v.numpy() for k, v in initial.items()}
+    rounds = [(list(range(6)), [5, 4, 3, 2, 1, 0], 3, [2]), ([0, 1, 3, 4, 5], [1, 0, 3, 5, 4], 2, [0, 4]),
+              ([1, 3, 5], [3, 1, 5], 4, [])]
+    for n, (residual, owners, width, finish) in enumerate(rounds):
+        rows = len(residual)
+        tree = torch.from_numpy(rng.randn(rows, tree_rows, dim).astype(np.float16))
+        index = torch.from_numpy(np.stack([np.sort(rng.choice(tree_rows, width, replace=False))
+                                           for _ in range(rows)]).astype(np.int64))
+        next_token = torch.from_numpy(rng.randint(0, 1000, size=(rows, width)))
+        gathered = tree.gather(dim=1, index=index.unsqueeze(-1).expand(rows, -1, dim))
+        hist.append(residual, {'generated_ids': next_token, 'features': gathered, 'input_ids': next_token},
+                    owners=torch.tensor(owners))
+        for row in finish:
+            hist.mark_finished(row)
+        out.update({f'r{n}_residual': np.array(residual), f'r{n}_owners': np.array(owners), f'r{n}_tree': tree.numpy(),
+                    f'r{n}_index': index.numpy(), f'r{n}_next_token': next_token.numpy(),
+                    f'r{n}_gathered': gathered.numpy(), f'r{n}_finish': np.array(finish, dtype=np.int64),
+                    f'r{n}_capacities': np.array([hist.capacities[k] for k in ('generated_ids', 'features',
+                                                                                  'input_ids')])})
+    final = hist.finalize()
+    for name in ('generated_ids', 'features', 'input_ids'):
+        out[f'final_{name}_lengths'] = np.array([len(r[name]) for r in final])
+        out[f'final_{name}'] = np.concatenate([r[name].numpy() for r in final])
+    save('history', rounds=len(rounds), repeats=repeats, max_length=6, **out)
+
+
 if __name__ == '__main__':
     torch.manual_seed(0)
     kv_sequence()
@@ -398,3 +438,4 @@ if __name__ == '__main__':
     tree_cases()
     attention_cases()
     draft_mask_cases()
+    history_cases()
