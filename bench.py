@@ -21,6 +21,8 @@ Reported (one JSON line on rank 0):
   cpu_baseline  the CPU oracle on a bounded sample of the same work
   draft_step   one draft expansion step (mask + attention of one draft layer),
              this library's launches beside the reference's torch sequence
+  history_step the accepted-feature gather + rollout-history append of a round,
+             one launch beside the reference's gather + index_copy_ sequence
 
 ``--impl reference`` times the CPU restatement of the reference's path (the
 reference is Python/torch and cannot run on the GPU host) on the host cores.
@@ -377,6 +379,7 @@ def run_ours(args):
 
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
     draft = measure_draft(st) if rank == 0 else None
+    history = measure_history(st) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
     append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
     append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
@@ -410,6 +413,7 @@ def run_ours(args):
         'clocks': clock,
         'e2e': e2e,
         'draft_step': draft,
+        'history_step': history,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(wl, budget_s=12.0)
@@ -485,6 +489,63 @@ def measure_draft(st, iters=20, warmup=3):
            'mask_bit_exact_vs_torch_sequence': same}
     del pool_k, pool_v
     return out
+
+
+def measure_history(st, iters=20, warmup=3, hidden=2048):
+    """The verify round's history step at the workload's batch (two responses per prompt):
+    gather of the accepted target features (hidden size `hidden`, bf16) from the tree's
+    hidden states and their append with the emitted tokens to the rollout-history pools,
+    as this library's one launch (ContiguousRolloutHistory.append_accepted) and as the
+    reference's torch sequence (gather, then one index_copy_ per field,
+    helper/opd_generate.py:567-579, helper/opd_history.py:24-42). Device time per step from
+    CUDA events around `iters` back-to-back steps."""
+    import torch
+    from analysis_spec_b200.opd_history import ContiguousRolloutHistory
+    wl, dev, dtype = st.wl, st.device, st.dtype
+    B, R, W = wl.batch, wl.rows, wl.depth + 1
+    gen = torch.Generator(device=dev).manual_seed(13)
+    init = {'generated_ids': torch.randint(0, 150000, (B // 2, 1), device=dev, generator=gen),
+            'features': torch.randn(B // 2, 1, hidden, device=dev, generator=gen).to(dtype),
+            'input_ids': torch.randint(0, 150000, (B // 2, 1), device=dev, generator=gen)}
+    cap = 1 + (iters + warmup) * W * 2 + W
+    ours = ContiguousRolloutHistory(init, repeats=2, max_length=cap)
+    pools = {k: v.clone() for k, v in ours.buffers.items()}
+    tree = torch.randn(B, R, hidden, device=dev, generator=gen).to(dtype)
+    index = torch.sort(torch.rand(B, R, device=dev, generator=gen).argsort(dim=1)[:, :W], dim=1).values
+    tok = torch.randint(0, 150000, (B, W), device=dev, generator=gen)
+    owners = torch.randperm(B, device=dev, generator=gen)
+    rows = owners.tolist()
+    state = {'start': 1}
+
+    def ours_step():
+        ours.append_accepted(rows, tok, tree, index, owners=owners)
+
+    def torch_step():
+        start = state['start']
+        feats = tree.gather(dim=1, index=index.unsqueeze(-1).expand(B, -1, hidden))
+        for name, chunk in (('generated_ids', tok), ('features', feats), ('input_ids', tok)):
+            pools[name][:, start:start + W].index_copy_(0, owners, chunk)
+        state['start'] = start + W
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1e3 / iters
+
+    t_ours, t_torch = timed(ours_step), timed(torch_step)
+    es = torch.finfo(dtype).bits // 8
+    moved = B * W * (hidden * es * 3 + 8 * 2 * 2)  # features read once, written twice; ids read + written
+    same = all(torch.equal(ours.buffers[k][:, :state['start']], pools[k][:, :state['start']]) for k in pools)
+    return {'shape': f'{B} rows, width {W}, {R}-row trees, hidden {hidden} {wl.dtype}', 'us': round(t_ours, 2),
+            'us_torch_sequence': round(t_torch, 2), 'bytes_per_step': moved,
+            'gbs': round(moved / (t_ours * 1e-6) / 1e9, 1), 'bit_exact_vs_torch_sequence': bool(same)}
 
 
 def measure_e2e(st, args, world):
