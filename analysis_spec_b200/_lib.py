@@ -51,6 +51,7 @@ SIGNATURES = {
     'speckv_causal_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_history_append': [_i32, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pi64, _pi64, _pi64, _pi64,
                               _p, _p, _i64, _i64, _p],
+    'speckv_mask_bits': [_p, _i32, _i64, _i64, _i64, _pi64, _p, _i64, _p, _p, _p],
     'speckv_history_pack': [_p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_expansion_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_version': [],

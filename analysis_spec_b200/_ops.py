@@ -304,6 +304,7 @@ def tree_mask(parents, past, steps, mask, pad=None):
         pad_stride = pad.stride(0)
     _lib.call('speckv_tree_mask', parents.data_ptr(), batch, rows, int(past), int(steps), mask.data_ptr(),
               _DTYPE_CODE[mask.dtype], _ptr(pad), pad_stride, _stream(parents))
+    torch.autograd.graph.increment_version(mask)
 
 
 def position_update(newly_padded, past, positions, past_positions, pad_rows=None, owners=None, pad_live=None):
@@ -436,6 +437,7 @@ def causal_mask(mask, past, pad=None):
     batch, _, query, columns = mask.shape
     _lib.call('speckv_causal_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, int(past), columns,
               _ptr(pad), ps0, ps1, _stream(mask))
+    torch.autograd.graph.increment_version(mask)
 
 
 def expansion_mask(mask, init_length, seen, pad=None):
@@ -448,6 +450,7 @@ def expansion_mask(mask, init_length, seen, pad=None):
         raise ValueError('expansion_mask: seen must be an int64 (batch, query[, 1]) tensor')
     _lib.call('speckv_expansion_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, columns,
               int(init_length), seen.data_ptr(), seen.stride(0), seen.stride(1), _ptr(pad), ps0, ps1, _stream(mask))
+    torch.autograd.graph.increment_version(mask)
 
 
 def _position_layout(fn, t):
@@ -520,3 +523,19 @@ def history_pack(dst, pool, offsets, rows, max_length):
         raise ValueError('history_pack: offsets must be contiguous int64 with rows + 1 entries')
     _lib.call('speckv_history_pack', dst.data_ptr(), pool.data_ptr(), pr, pp, rb, offsets.data_ptr(), int(rows),
               int(max_length), _stream(pool))
+
+
+def mask_bits(mask, bits, first_col, nonbinary):
+    """Visibility bits of a dense additive (batch, 1, rows, columns) mask (any strides): bit set
+    iff the entry is 0; lowest-value / -inf entries masked; any other value sets nonbinary[0]."""
+    _require_cuda(mask, bits, first_col, nonbinary)
+    if mask.dim() != 4 or mask.shape[1] != 1 or mask.dtype not in _DTYPE_CODE:
+        raise ValueError('mask_bits: mask must be a float (batch, 1, rows, columns) tensor')
+    batch, _, rows, cols = mask.shape
+    if bits.dtype != torch.int32 or not bits.is_contiguous() or tuple(bits.shape[:2]) != (batch, rows):
+        raise ValueError('mask_bits: bits must be a contiguous (batch, rows, words) int32 tensor')
+    if first_col.dtype != torch.int32 or first_col.numel() < batch or nonbinary.dtype != torch.int32:
+        raise ValueError('mask_bits: first_col / nonbinary must be int32')
+    _lib.call('speckv_mask_bits', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, rows, cols,
+              _lib.i64_array([mask.stride(0), mask.stride(2), mask.stride(3)]), bits.data_ptr(), bits.shape[2],
+              first_col.data_ptr(), nonbinary.data_ptr(), _stream(mask))

@@ -60,6 +60,8 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--layers', type=int, default=None, help='override the layer count (small profiling cases)')
     p.add_argument('--batch', type=int, default=None, help='override the per-GPU batch (small profiling cases)')
+    p.add_argument('--side-only', action='store_true',
+                   help='only the draft-step and history-step measurements, on a one-layer cache (profiling)')
     return p.parse_args()
 
 
@@ -305,6 +307,24 @@ def verify_round(st, i, marks=None):
     extension = min(r[2] for r in live) if live else width
     st.cache.crop(st.past)  # stationary workload: the next round verifies at the same length
     return width, extension, rows
+
+
+def run_side(args):
+    """The draft-step and history-step measurements alone, on a one-layer cache of the workload
+    (a small device footprint for kernel profiling); prints one JSON line."""
+    import torch
+    from dataclasses import replace
+    from analysis_spec_b200 import _lib
+    from analysis_spec_b200.build import build
+    build()
+    device = torch.device('cuda', 0)
+    torch.cuda.set_device(device)
+    _lib.load()
+    wl = replace(workload(args), layers=1)
+    st = Round(wl, device, seed=1000)
+    print(json.dumps({'impl': 'ours', 'side_only': True, 'config': workload_config(wl),
+                      'draft_step': measure_draft(st, iters=args.steps, warmup=args.warmup),
+                      'history_step': measure_history(st, iters=args.steps, warmup=args.warmup)}), flush=True)
 
 
 def run_ours(args):
@@ -718,5 +738,7 @@ if __name__ == '__main__':
     a = parse()
     if a.impl == 'reference':
         run_reference(a)
+    elif a.side_only:
+        run_side(a)
     else:
         run_ours(a)

@@ -370,6 +370,19 @@ int speckv_tree_mask_bits(const int64_t* parents, int64_t batch, int64_t rows, i
                           const uint8_t* pad, int64_t pad_stride_b, uint32_t* bits, int64_t row_words,
                           int32_t* first_col, void* stream);
 
+/* Visibility bits of a dense additive mask (batch, 1, rows, columns) with element
+ * strides mask_strides = (b, r, c): bit set iff the entry is 0; entries equal to
+ * the dtype's lowest finite value or -inf are masked; any other value sets
+ * *nonbinary = 1 (device int32) and the bits must not be used. first_col[b] =
+ * the first column any row of sequence b sees (0x7f7f7f7f when none). bits,
+ * row_words and first_col as for speckv_tree_mask_bits. Lets the drop-in
+ * attention convert transformers' per-forward 4-D mask (built once, read by every
+ * layer, integrations/sdpa_attention.py:40-104) once into the form
+ * speckv_tree_attention_bits reads. */
+int speckv_mask_bits(const void* mask, int32_t dtype, int64_t batch, int64_t rows, int64_t columns,
+                     const int64_t* mask_strides, uint32_t* bits, int64_t row_words, int32_t* first_col,
+                     int32_t* nonbinary, void* stream);
+
 /* speckv_tree_attention with visibility taken from speckv_tree_mask_bits output
  * instead of a dense mask (masked scores contribute exactly 0). first_col may
  * be NULL. */

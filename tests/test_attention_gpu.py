@@ -185,3 +185,51 @@ def test_registered_interface_and_no_mask():
                               128 ** -0.5)
     assert weights is None
     check(out, expect)
+
+
+@pytest.mark.parametrize('batch,hq,hkv,rows,past', [(4, 16, 2, 61, 300), (3, 28, 4, 17, 1100), (2, 16, 2, 1, 257)])
+def test_dense_mask_runs_the_bits_kernel(batch, hq, hkv, rows, past):
+    """A dense 0 / lowest-value mask (the drop-in path) is converted once into visibility bits
+    identical to tree_mask_bits' and every later call with the same mask reuses them."""
+    from analysis_spec_b200.tree_attention import dense_mask_visibility
+    q, k, v, mask, parents, pad = random_case(batch, hq, hkv, rows, past, 128, seed=rows + past)
+    out, _ = tree_verify_attention(Module(hq // hkv), q, k, v, mask, scaling=128 ** -0.5)
+    key, dense = mask._speckv_dense_bits
+    assert dense is not None
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(parents).cuda(),
+                      torch.from_numpy(parents).cuda(), rows)
+    vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+    assert torch.equal(dense.bits, vis.bits)
+    assert torch.equal(dense.first_col, vis.first_col)
+    vis_np = oracle.tree_visible(parents, past, rows, pad=pad)
+    expect = oracle.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                              oracle.additive_mask(vis_np, 'bfloat16'), 128 ** -0.5)
+    check(out, expect)
+    # a second layer of the same forward: no new conversion
+    tree_verify_attention(Module(hq // hkv), q, k, v, mask, scaling=128 ** -0.5)
+    assert mask._speckv_dense_bits[1] is dense
+    assert dense_mask_visibility(mask, mask, batch, rows, past + rows) is dense
+    # an in-place change of the mask invalidates the cached bits
+    mask[:, :, :, past + rows - 1] = torch.finfo(mask.dtype).min
+    out2, _ = tree_verify_attention(Module(hq // hkv), q, k, v, mask, scaling=128 ** -0.5)
+    assert mask._speckv_dense_bits[1] is not dense
+    vis_np[:, :, past + rows - 1] = False
+    if vis_np.any(axis=-1).all():
+        expect = oracle.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                                  oracle.additive_mask(vis_np, 'bfloat16'), 128 ** -0.5)
+        check(out2, expect)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
+def test_non_binary_mask_keeps_the_dense_kernel():
+    q, k, v, mask, parents, pad = random_case(3, 16, 2, 17, 200, 128, seed=3)
+    soft = mask.clone()
+    soft[:, :, :, 200] = -2.5  # the root's column, visible to every tree row: a soft bias
+    out, _ = tree_verify_attention(Module(8), q, k, v, soft, scaling=128 ** -0.5)
+    assert soft._speckv_dense_bits[1] is None
+    expect = oracle.attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                              soft.float().cpu().numpy(), 128 ** -0.5)
+    check(out, expect)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
