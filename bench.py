@@ -443,13 +443,45 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+def time_steps(fn, iters, warmup, spin_ms=8.0):
+    """(device µs, launch-bound µs) per call of `fn`. Device: the `iters` calls are queued
+    behind a GPU spin of `spin_ms` so the host enqueues them all before the GPU reaches the
+    first, and the CUDA events around them see device time only (None if enqueueing took
+    longer than the spin). Launch-bound: the same calls back to back on an idle GPU, host
+    launch cost included."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(spin_ms * 1e-3 * 2.0e9))
+    t0 = time.perf_counter()
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    host_ms = (time.perf_counter() - t0) * 1e3
+    torch.cuda.synchronize()
+    device = a.elapsed_time(b) * 1e3 / iters if host_ms < 0.8 * spin_ms else None
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return device, a.elapsed_time(b) * 1e3 / iters
+
+
+def _r(x):
+    return None if x is None else round(x, 2)
+
+
 def measure_draft(st, iters=20, warmup=3):
     """One draft expansion step of one draft layer at the workload's batch, heads and shared
     past (draft K = the tree's top-k): the expansion mask and the draft attention, each as
     this library's launch and as the reference's torch sequence on the same GPU (zero /
     [init:] fill / scatter / padding fill, helper/opd_generate.py:143-162; repeat_kv + SDPA,
-    helper/fastgrpo_model.py:58-69). Device time per step from CUDA events around `iters`
-    back-to-back steps; the K/V views (> L2) are strided cache views."""
+    helper/fastgrpo_model.py:58-69), each timed by time_steps; the K/V views (> L2) are
+    strided cache views."""
     import torch
     import torch.nn.functional as F
     from analysis_spec_b200.draft_attention import draft_sdpa
@@ -487,25 +519,18 @@ def measure_draft(st, iters=20, warmup=3):
         vv = values[:, :, None].expand(B, Hkv, g, cols, D).reshape(B, Hq, cols, D)
         F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask)
 
-    def timed(fn):
-        for _ in range(warmup):
-            fn()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        a.record()
-        for _ in range(iters):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) * 1e3 / iters
-
     torch_mask()
     ref_mask = mask.clone()
     ours_mask()
     same = bool(torch.equal(mask.view(torch.int16), ref_mask.view(torch.int16)))
+    t = {name: time_steps(fn, iters, warmup) for name, fn in
+         (('mask', ours_mask), ('mask_torch', torch_mask), ('attn', ours_attn), ('attn_torch', torch_attn))}
     out = {'shape': f'batch {B}, draft_k {k}, columns {cols}, {Hq}q/{Hkv}kv x {D}, one draft layer',
-           'mask_us': round(timed(ours_mask), 2), 'mask_us_torch_sequence': round(timed(torch_mask), 2),
-           'attention_us': round(timed(ours_attn), 2), 'attention_us_torch_sdpa': round(timed(torch_attn), 2),
+           'mask_us': _r(t['mask'][0]), 'mask_us_torch_sequence': _r(t['mask_torch'][0]),
+           'attention_us': _r(t['attn'][0]), 'attention_us_torch_sdpa': _r(t['attn_torch'][0]),
+           'launch_bound_us': {k2: _r(v[1]) for k2, v in t.items()},
+           'timing': 'device time per step (steps queued behind a GPU spin); launch_bound_us: back to back on an '
+                     'idle GPU, host launch cost included',
            'mask_bit_exact_vs_torch_sequence': same}
     del pool_k, pool_v
     return out
@@ -517,8 +542,7 @@ def measure_history(st, iters=20, warmup=3, hidden=2048):
     hidden states and their append with the emitted tokens to the rollout-history pools,
     as this library's one launch (ContiguousRolloutHistory.append_accepted) and as the
     reference's torch sequence (gather, then one index_copy_ per field,
-    helper/opd_generate.py:567-579, helper/opd_history.py:24-42). Device time per step from
-    CUDA events around `iters` back-to-back steps."""
+    helper/opd_generate.py:567-579, helper/opd_history.py:24-42), each timed by time_steps."""
     import torch
     from analysis_spec_b200.opd_history import ContiguousRolloutHistory
     wl, dev, dtype = st.wl, st.device, st.dtype
@@ -527,7 +551,7 @@ def measure_history(st, iters=20, warmup=3, hidden=2048):
     init = {'generated_ids': torch.randint(0, 150000, (B // 2, 1), device=dev, generator=gen),
             'features': torch.randn(B // 2, 1, hidden, device=dev, generator=gen).to(dtype),
             'input_ids': torch.randint(0, 150000, (B // 2, 1), device=dev, generator=gen)}
-    cap = 1 + (iters + warmup) * W * 2 + W
+    cap = 1 + (warmup + 2 * iters) * W + W
     ours = ContiguousRolloutHistory(init, repeats=2, max_length=cap)
     pools = {k: v.clone() for k, v in ours.buffers.items()}
     tree = torch.randn(B, R, hidden, device=dev, generator=gen).to(dtype)
@@ -547,25 +571,18 @@ def measure_history(st, iters=20, warmup=3, hidden=2048):
             pools[name][:, start:start + W].index_copy_(0, owners, chunk)
         state['start'] = start + W
 
-    def timed(fn):
-        for _ in range(warmup):
-            fn()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        a.record()
-        for _ in range(iters):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) * 1e3 / iters
-
-    t_ours, t_torch = timed(ours_step), timed(torch_step)
+    (t_ours, lb_ours), (t_torch, lb_torch) = time_steps(ours_step, iters, warmup), time_steps(torch_step, iters,
+                                                                                               warmup)
     es = torch.finfo(dtype).bits // 8
     moved = B * W * (hidden * es * 3 + 8 * 2 * 2)  # features read once, written twice; ids read + written
     same = all(torch.equal(ours.buffers[k][:, :state['start']], pools[k][:, :state['start']]) for k in pools)
-    return {'shape': f'{B} rows, width {W}, {R}-row trees, hidden {hidden} {wl.dtype}', 'us': round(t_ours, 2),
-            'us_torch_sequence': round(t_torch, 2), 'bytes_per_step': moved,
-            'gbs': round(moved / (t_ours * 1e-6) / 1e9, 1), 'bit_exact_vs_torch_sequence': bool(same)}
+    return {'shape': f'{B} rows, width {W}, {R}-row trees, hidden {hidden} {wl.dtype}', 'us': _r(t_ours),
+            'us_torch_sequence': _r(t_torch), 'bytes_per_step': moved,
+            'gbs': None if t_ours is None else round(moved / (t_ours * 1e-6) / 1e9, 1),
+            'launch_bound_us': {'ours': _r(lb_ours), 'torch_sequence': _r(lb_torch)},
+            'timing': 'device time per step (steps queued behind a GPU spin); launch_bound_us: back to back on an '
+                      'idle GPU, host launch cost included',
+            'bit_exact_vs_torch_sequence': bool(same)}
 
 
 def measure_e2e(st, args, world):
