@@ -48,12 +48,12 @@ SIGNATURES = {
                               ctypes.c_float, _i32, _p],
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],
     'speckv_plan_launch': [_p, _p],
-    'speckv_causal_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p],
+    'speckv_causal_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p],
     'speckv_history_append': [_i32, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pp, _pi64, _pi64, _pi64, _pi64, _pi64,
                               _p, _p, _i64, _i64, _p],
     'speckv_mask_bits': [_p, _i32, _i64, _i64, _i64, _pi64, _p, _i64, _p, _p, _p],
     'speckv_history_pack': [_p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p],
-    'speckv_expansion_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p],
+    'speckv_expansion_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p],
     'speckv_version': [],
 }
 

@@ -430,26 +430,42 @@ def _mask_operands(fn, mask, pad):
     return pad.stride(0), pad.stride(1)
 
 
-def causal_mask(mask, past, pad=None):
-    """mask[b, 0, r, c] = 0 if c <= past + r and not pad[b, c] else finfo(dtype).min (one launch)."""
-    _require_cuda(mask, pad)
+def _bits_operands(fn, mask, bits, first_col):
+    if bits is None:
+        return 0
+    batch, _, query, columns = mask.shape
+    if bits.dtype != torch.int32 or not bits.is_contiguous() or tuple(bits.shape[:2]) != (batch, query) or \
+            bits.shape[2] < visibility_words(columns):
+        raise ValueError(f'{fn}: bits must be a contiguous (batch, query, >= 4 * ceil(columns / 128)) int32 tensor')
+    if first_col is None or first_col.dtype != torch.int32 or first_col.numel() < batch:
+        raise ValueError(f'{fn}: first_col must be an int32 tensor of batch entries')
+    return bits.shape[2]
+
+
+def causal_mask(mask, past, pad=None, bits=None, first_col=None):
+    """mask[b, 0, r, c] = 0 if c <= past + r and not pad[b, c] else finfo(dtype).min (one launch);
+    with `bits` / `first_col` the same visibility bit-packed for tree_attention_bits."""
+    _require_cuda(mask, pad, bits, first_col)
     ps0, ps1 = _mask_operands('causal_mask', mask, pad)
+    words = _bits_operands('causal_mask', mask, bits, first_col)
     batch, _, query, columns = mask.shape
     _lib.call('speckv_causal_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, int(past), columns,
-              _ptr(pad), ps0, ps1, _stream(mask))
+              _ptr(pad), ps0, ps1, _ptr(bits), words, _ptr(first_col), _stream(mask))
     torch.autograd.graph.increment_version(mask)
 
 
-def expansion_mask(mask, init_length, seen, pad=None):
+def expansion_mask(mask, init_length, seen, pad=None, bits=None, first_col=None):
     """mask[b, 0, r, c] = 0 if (c < init_length or c == seen[b, r, 0]) and not pad[b, c], else
     finfo(dtype).min; `seen` (batch, query[, 1]) int64 (one launch)."""
-    _require_cuda(mask, seen, pad)
+    _require_cuda(mask, seen, pad, bits, first_col)
     ps0, ps1 = _mask_operands('expansion_mask', mask, pad)
+    words = _bits_operands('expansion_mask', mask, bits, first_col)
     batch, _, query, columns = mask.shape
     if seen.dtype != torch.long or seen.shape[0] < batch or seen.shape[1] < query:
         raise ValueError('expansion_mask: seen must be an int64 (batch, query[, 1]) tensor')
     _lib.call('speckv_expansion_mask', mask.data_ptr(), _DTYPE_CODE[mask.dtype], batch, query, columns,
-              int(init_length), seen.data_ptr(), seen.stride(0), seen.stride(1), _ptr(pad), ps0, ps1, _stream(mask))
+              int(init_length), seen.data_ptr(), seen.stride(0), seen.stride(1), _ptr(pad), ps0, ps1, _ptr(bits),
+              words, _ptr(first_col), _stream(mask))
     torch.autograd.graph.increment_version(mask)
 
 

@@ -6,10 +6,34 @@ dtype), grown to a power of two of at least 256 elements, ``allocations`` counti
 growths; helper/opd_attention.py:5-47); its CUDA causal mask is one libspeckv launch.
 ``expansion_mask`` replaces the zero / fill / scatter / padding sequence of
 helper/opd_generate.py:143-162 with one launch.
+
+Both masks are returned carrying their visibility bits (written by the same launch), so
+the draft attention (``draft_attention.draft_sdpa``) runs the bits tensor-core kernel
+without reading the dense mask or converting it. The bits buffers are private to this
+module and not counted in ``allocations`` / ``memory_bytes()``, which follow the
+reference's accounting of the mask buffers.
 """
 import torch
 
 from . import _ops, opd_attention_kernels
+from .tree_attention import DenseMaskVisibility
+
+
+def _attach_visibility(mask, bits, first_col):
+    batch, _, query, columns = mask.shape
+    mask._speckv_dense_bits = ((columns, query, batch, mask._version), DenseMaskVisibility(bits, first_col))
+    return mask
+
+
+def _visibility_buffers(store, name, batch, query, columns, device):
+    words = _ops.visibility_words(columns)
+    count = batch * query * words
+    key = (name, 'bits')
+    pool = store.get(key)
+    if pool is None or pool.numel() < count + batch:
+        pool = torch.empty(_capacity(count + batch), dtype=torch.int32, device=device)
+        store[key] = pool
+    return pool[:count].view(batch, query, words), pool[count:count + batch]
 
 
 def _capacity(count):
@@ -49,8 +73,11 @@ class AttentionWorkspace:
         """Causal mask (batch, 1, query, past + query) in the workspace buffer ``name``: one
         libspeckv launch; a workspace on a non-CUDA device raises (no CPU path)."""
         out = self.buffer(name, (batch, 1, query, past + query), dtype)
-        opd_attention_kernels.causal_mask(out, past, padding)
-        return out
+        if not hasattr(self, '_visibility'):
+            self._visibility = {}
+        bits, first = _visibility_buffers(self._visibility, name, batch, query, past + query, out.device)
+        _ops.causal_mask(out, past, padding, bits, first)
+        return _attach_visibility(out, bits, first)
 
     def memory_bytes(self):
         return sum(t.numel() * t.element_size() for t in self.buffers.values())
@@ -66,7 +93,10 @@ def expansion_mask(mask, init_length, seen, padding=None):
         pairs = [[b, int(c)] for b, cols in enumerate(padding) for c in cols]
         padding = torch.tensor(pairs, device=mask.device, dtype=torch.long) if pairs else None
     pad = padding if isinstance(padding, torch.Tensor) and padding.dtype == torch.bool else None
-    _ops.expansion_mask(mask, init_length, seen, pad)
+    batch, _, query, columns = mask.shape
+    bits, first = _visibility_buffers({}, None, batch, query, columns, mask.device)
+    _ops.expansion_mask(mask, init_length, seen, pad, bits, first)
+    _attach_visibility(mask, bits, first)  # a pairs-form fill below advances the version: bits dropped
     if isinstance(padding, torch.Tensor) and padding.dtype != torch.bool and padding.numel():
         mask[padding[:, 0], 0, :, padding[:, 1]] = torch.finfo(mask.dtype).min
     return mask

@@ -134,7 +134,7 @@ int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_
  * (helper/opd_attention_kernels.py:7-22). */
 int speckv_causal_mask(void* mask, int32_t dtype, int64_t batch, int64_t query, int64_t past,
                        int64_t columns, const uint8_t* pad, int64_t pad_stride_b, int64_t pad_stride_c,
-                       void* stream);
+                       uint32_t* bits, int64_t row_words, int32_t* first_col, void* stream);
 
 /* Draft expansion mask (batch, 1, query, columns), contiguous: entry (b, r, c) is 0
  * when (c < init_length or c == seen[b][r]) and pad[b][c] is false, else the dtype's
@@ -146,7 +146,14 @@ int speckv_causal_mask(void* mask, int32_t dtype, int64_t batch, int64_t query, 
 int speckv_expansion_mask(void* mask, int32_t dtype, int64_t batch, int64_t query, int64_t columns,
                           int64_t init_length, const int64_t* seen, int64_t seen_stride_b,
                           int64_t seen_stride_r, const uint8_t* pad, int64_t pad_stride_b,
-                          int64_t pad_stride_c, void* stream);
+                          int64_t pad_stride_c, uint32_t* bits, int64_t row_words, int32_t* first_col,
+                          void* stream);
+
+/* Both mask entries optionally (bits non-NULL) also write the mask's visibility in
+ * the form speckv_tree_attention_bits reads: bits[b * query + r][w] bit i = entry
+ * (b, r, 32 w + i) is 0; row_words >= 4 * ceil(columns / 128), words past the last
+ * column 0; first_col[b] = the first column any row of sequence b sees
+ * (0x7f7f7f7f when none). The draft attention then skips the dense mask read. */
 
 /* ---- Rollout history ---------------------------------------------------- */
 

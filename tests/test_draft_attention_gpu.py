@@ -96,3 +96,29 @@ def test_draft_sdpa_argument_checks():
         draft_sdpa(q, k, k, torch.zeros(1, 1, 2, 5, device='cuda', dtype=torch.bfloat16), 3)
     with pytest.raises(ValueError):
         draft_sdpa(q, k, k, torch.zeros(1, 1, 2, 5, device='cuda', dtype=torch.bfloat16), 2, dropout_p=0.1)
+
+
+def test_draft_expansion_pairs_padding_and_foreign_mask():
+    """Pairs-form padding (filled after the mask kernel) and a mask built outside this
+    library both reach the right visibility."""
+    batch, hq, hkv, past, draft_k, init, dim, dtype = 3, 16, 2, 300, 6, 280, 128, torch.bfloat16
+    rng = np.random.RandomState(4)
+    gen = torch.Generator(device='cuda').manual_seed(4)
+    cache, pad = draft_cache(batch, hkv, past, dim, dtype, gen, rng)
+    new = [(0.5 * torch.randn(batch, hkv, draft_k, dim, device='cuda', generator=gen)).to(dtype) for _ in range(2)]
+    keys, values = cache.update(new[0], new[1], 0)
+    cols = past + draft_k
+    seen = torch.from_numpy(rng.randint(init, cols, size=(batch, draft_k, 1)).astype(np.int64)).cuda()
+    pairs = np.array([[b, c] for b in range(batch) for c in rng.choice(init, 5, replace=False)], dtype=np.int64)
+    mask = torch.empty(batch, 1, draft_k, cols, device='cuda', dtype=dtype)
+    expansion_mask(mask, init, seen, torch.from_numpy(pairs).cuda())
+    q = (0.5 * torch.randn(batch, hq, draft_k, dim, device='cuda', generator=gen)).to(dtype)
+    out = draft_sdpa(q, keys, values, mask, hq // hkv)
+    vis = oracle.expansion_visible(batch, draft_k, cols, init, seen.cpu().numpy(), pad_pairs=pairs)
+    check(out, q, keys, values, vis, dtype)
+    foreign = mask.clone()  # no attached bits: converted once, then cached
+    out2 = draft_sdpa(q, keys, values, foreign, hq // hkv)
+    assert foreign._speckv_dense_bits[1] is not None
+    check(out2, q, keys, values, vis, dtype)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None

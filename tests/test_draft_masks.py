@@ -168,3 +168,40 @@ def test_masks_empty_and_invalid_arguments():
         causal_mask(torch.empty(2, 1, 4, 8, device='cuda'), -1)
     torch.cuda.synchronize()
     assert _ops.device_error() is None
+
+
+def unpack_bits(bits, columns):
+    words = bits.cpu().numpy().view(np.uint32)
+    unpacked = np.unpackbits(words.view(np.uint8), bitorder='little').reshape(words.shape[0], words.shape[1], -1)
+    assert not unpacked[:, :, columns:].any()
+    return unpacked[:, :, :columns].astype(bool)
+
+
+@pytest.mark.gpu
+def test_masks_carry_their_visibility_bits(golden):
+    """The bits written beside each mask (what the draft attention reads) match the mask."""
+    from analysis_spec_b200 import _ops
+    from analysis_spec_b200.opd_attention import AttentionWorkspace, expansion_mask
+    g = golden('draft_masks')
+    ws = AttentionWorkspace('cuda')
+    for batch, query, past, dtype, pad, visible in causal_cases(g):
+        padding = None if pad is None else torch.from_numpy(pad).cuda()
+        out = ws.causal('draft_causal', past, query, batch, dtype, padding)
+        key, vis = out._speckv_dense_bits
+        assert key == (past + query, query, batch, out._version)
+        assert np.array_equal(unpack_bits(vis.bits, past + query), visible)
+        assert np.array_equal(vis.first_col.cpu().numpy(), visible.any(axis=1).argmax(axis=1))
+    for batch, k, cols, init, dtype, seen, pad, pairs, visible in expansion_cases(g):
+        mask = ws.buffer('draft_expansion', (batch, 1, k, cols), dtype)
+        padding = torch.from_numpy(pad).cuda() if pad is not None else (
+            torch.from_numpy(pairs).cuda() if pairs is not None else None)
+        expansion_mask(mask, init, torch.from_numpy(seen).cuda(), padding)
+        key, vis = mask._speckv_dense_bits
+        if pairs is not None:  # filled after the kernel: the attached bits are stale by version
+            assert key[3] != mask._version
+            continue
+        assert key[3] == mask._version
+        assert np.array_equal(unpack_bits(vis.bits, cols), visible)
+        assert np.array_equal(vis.first_col.cpu().numpy(), visible.any(axis=1).argmax(axis=1))
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
