@@ -481,14 +481,46 @@ def _position_layout(fn, t):
     return t.stride(0) * es, t.stride(1) * es, expect * es
 
 
-def history_append(fields, owners, pool_rows, n, src_rows=None):
+def _history_layout_key(fields, n, pool_rows):
+    key = [n, pool_rows]
+    for pool, src, index, gathered, start, width in fields:
+        key.append((0 if pool is None else pool.data_ptr(), None if pool is None else (pool.shape, pool.stride()),
+                    src.dtype, src.shape, src.stride(), None if index is None else (index.dtype, index.shape, index.stride()),
+                    None if gathered is None else (gathered.dtype, gathered.shape, gathered.is_contiguous()), width))
+    return tuple(key)
+
+
+def history_append(fields, owners, pool_rows, n, src_rows=None, cache=None):
     """One launch over up to four history fields. Each field is a tuple
     (pool, src, index, gathered, start, width): pool (pool_rows, capacity, *elem) or None;
     src (rows, positions, *elem); index int64 (n, width) source positions or None (w);
     gathered contiguous (n, width, *elem) or None. owners int64 (n,) pool rows;
-    src_rows int64 (n,) source rows or None (i)."""
+    src_rows int64 (n,) source rows or None (i). `cache` (a dict the caller keeps) holds the
+    packed argument arrays of each layout seen (pools, shapes, strides, widths): a later call
+    with the same layout only refreshes the source, index, output pointers and starts."""
     if not 1 <= len(fields) <= 4:
         raise ValueError('history_append: 1..4 fields')
+    _require_cuda(owners, src_rows)
+    for t in (owners, src_rows):
+        if t is not None and (t.dtype != torch.long or not t.is_contiguous() or t.numel() < n):
+            raise ValueError('history_append: owners / src_rows must be contiguous int64 with n entries')
+    key = None
+    if cache is not None:
+        key = _history_layout_key(fields, n, pool_rows)
+        packed = cache.get(key)
+        if packed is not None:
+            args, srcs, idx, gath, starts = packed
+            for f, (pool, src, index, gathered, start, width) in enumerate(fields):
+                if not src.is_cuda or (index is not None and not index.is_cuda) or \
+                        (gathered is not None and not gathered.is_cuda):
+                    raise RuntimeError('analysis_spec_b200 kernels need CUDA tensors (the product has no CPU path)')
+                srcs[f] = src.data_ptr()
+                idx[f] = _ptr(index)
+                gath[f] = _ptr(gathered)
+                starts[f] = int(start)
+            _lib.call('speckv_history_append', *args, _ptr(owners), _ptr(src_rows), int(n), int(pool_rows),
+                      _stream(fields[0][1]))
+            return
     pools, pstr, srcs, sstr, idx, istr, gath, rbytes, spos, starts, widths, caps = ([] for _ in range(12))
     for pool, src, index, gathered, start, width in fields:
         _require_cuda(pool, src, index, gathered)
@@ -517,16 +549,17 @@ def history_append(fields, owners, pool_rows, n, src_rows=None):
         starts.append(int(start))
         widths.append(int(width))
         caps.append(pool.shape[1] if pool is not None else 0)
-    _require_cuda(owners, src_rows)
-    for t in (owners, src_rows):
-        if t is not None and (t.dtype != torch.long or not t.is_contiguous() or t.numel() < n):
-            raise ValueError('history_append: owners / src_rows must be contiguous int64 with n entries')
-    ref = fields[0][1]
-    _lib.call('speckv_history_append', len(fields), _lib.ptr_array(pools), _lib.i64_array(pstr),
-              _lib.ptr_array(srcs), _lib.i64_array(sstr), _lib.ptr_array(idx), _lib.i64_array(istr),
-              _lib.ptr_array(gath), _lib.i64_array(rbytes), _lib.i64_array(spos), _lib.i64_array(starts),
-              _lib.i64_array(widths), _lib.i64_array(caps), _ptr(owners), _ptr(src_rows), int(n), int(pool_rows),
-              _stream(ref))
+    srcs, idx, gath, starts = (_lib.ptr_array(srcs), _lib.ptr_array(idx), _lib.ptr_array(gath),
+                               _lib.i64_array(starts))
+    args = (len(fields), _lib.ptr_array(pools), _lib.i64_array(pstr), srcs, _lib.i64_array(sstr), idx,
+            _lib.i64_array(istr), gath, _lib.i64_array(rbytes), _lib.i64_array(spos), starts, _lib.i64_array(widths),
+            _lib.i64_array(caps))
+    if cache is not None:
+        if len(cache) >= 16:
+            cache.clear()
+        cache[key] = (args, srcs, idx, gath, starts)
+    _lib.call('speckv_history_append', *args, _ptr(owners), _ptr(src_rows), int(n), int(pool_rows),
+              _stream(fields[0][1]))
 
 
 def history_pack(dst, pool, offsets, rows, max_length):

@@ -38,6 +38,7 @@ class ContiguousRolloutHistory:
         self.lengths = {}
         self.capacities = {}
         self.finished = {}
+        self._launches = {}  # packed launch arguments per field layout (see _ops.history_append)
         fields = []
         for name, tensor in initial.items():
             length = tensor.shape[1]
@@ -90,7 +91,7 @@ class ContiguousRolloutHistory:
                 pool = self._grow(name, end)
             fields.append((pool, chunk, None, None, start, chunk.shape[1]))
         for group in _launch_groups(fields):
-            _ops.history_append(group, owners, self.response_count, n)
+            _ops.history_append(group, owners, self.response_count, n, cache=self._launches)
         for name, chunk in chunks.items():
             self.lengths[name] += chunk.shape[1]
 
@@ -133,7 +134,7 @@ class ContiguousRolloutHistory:
             if start + width > pool.shape[1]:
                 pool = self._grow('features', start + width)
         fields.append((pool, feature_tree, index, features_out, start, width))
-        _ops.history_append(fields, owners, self.response_count, n)
+        _ops.history_append(fields, owners, self.response_count, n, cache=self._launches)
         for name in names:
             self.lengths[name] += width
         return features_out
