@@ -640,7 +640,7 @@ __host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u;
 __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
 
 enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
-       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18 };
+       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19 };
 
 // Warp-wide forms: every lane runs the same code (the operands stay warp-uniform) and
 // one elected lane, always lane 0 with the full mask, issues the instruction; the
@@ -759,7 +759,12 @@ struct Item {
   int b, kvh, pair;
 };
 
-template <typename T>
+// SPLIT (at most 128 packed rows per (sequence, KV head), e.g. a draft step): both
+// softmax warpgroups serve the one Q tile and take alternate key tiles (warpgroup w the
+// tiles i with i % 2 == w); S_w of tile i and the P.V of tile i - 1 are issued in turn,
+// so the K and V rings are consumed in order. Warpgroup 1 hands its running max and sum
+// to warpgroup 0 through shared memory (C_XCHG, a bounded wait), which merges O0 and O1.
+template <typename T, bool SPLIT>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const Sm100Args a) {
@@ -798,6 +803,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mbar_init(bar(C_P_FULL + i), 128);
     }
     mbar_init(bar(C_DRAIN), 1);
+    mbar_init(bar(C_XCHG), 128);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -890,8 +896,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       constexpr uint64_t kStageStep = kTileBytes >> 4;
       // descriptors are computed by the whole warp (warp-uniform); one elected lane issues
       // the group of MMAs and its commit
-      auto issue_s = [&](int t, int stage) {
-        const uint64_t ad = q_desc + (uint64_t)t * kStageStep, bd = k_desc + (uint64_t)stage * kStageStep;
+      auto issue_s = [&](int t, int stage, int qt) {
+        const uint64_t ad = q_desc + (uint64_t)qt * kStageStep, bd = k_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + S_COL(t);
         const uint32_t sbar = bar(C_S_FULL + t);
         if (elect_one()) {
@@ -920,6 +926,41 @@ __global__ void __launch_bounds__(kThreads2, 1)
         return true;
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
+        if (SPLIT) {
+          const int n = n_tiles_all - first_tile(it.b);
+          ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
+          tc_fence_after();
+          int prev_stage = 0;
+          for (int i = 0; ok && i < n; ++i, ++cnt) {
+            const int s = cnt & 1, w = i & 1;
+            if (!wait(C_K_FULL + s, (cnt >> 1) & 1, 26)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(w, s, 0);
+            tc_commit_w(bar(C_K_EMPTY + s));
+            if (i > 0) {  // P.V of the previous tile, the other warpgroup's
+              if (!wait(C_V_FULL + prev_stage, ((cnt - 1) >> 1) & 1, 27)) { ok = false; break; }
+              tc_fence_after();
+              if (!issue_pv(1 - w, prev_stage, i - 1 < 2)) { ok = false; break; }
+              tc_commit_w(bar(C_V_EMPTY + prev_stage));
+            }
+            prev_stage = s;
+          }
+          if (ok && n > 0) {
+            if (!wait(C_V_FULL + prev_stage, ((cnt - 1) >> 1) & 1, 27)) {
+              ok = false;
+            } else {
+              tc_fence_after();
+              if (issue_pv((n - 1) & 1, prev_stage, n - 1 < 2)) tc_commit_w(bar(C_V_EMPTY + prev_stage));
+              else ok = false;
+            }
+          }
+          if (!ok) break;
+          tc_commit_w(bar(C_O_FINAL + 0));
+          tc_commit_w(bar(C_O_FINAL + 1));
+          ++ic[0];
+          ++ic[1];
+          continue;
+        }
         const bool act1 = it.pair * 2 * BM + BM < total_rows;
         const int n = n_tiles_all - first_tile(it.b);
         ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
@@ -930,12 +971,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
           const int s = cnt & 1;
           if (!wait(C_K_FULL + s, (cnt >> 1) & 1, 26)) { ok = false; break; }
           tc_fence_after();
-          issue_s(0, s);
+          issue_s(0, s, 0);
           if (act1 && i > 0) {
             if (!issue_pv(1, prev_stage, i == 1)) { ok = false; break; }
             tc_commit_w(bar(C_V_EMPTY + prev_stage));
           }
-          if (act1) issue_s(1, s);
+          if (act1) issue_s(1, s, 1);
           tc_commit_w(bar(C_K_EMPTY + s));
           if (!wait(C_V_FULL + s, (cnt >> 1) & 1, 27)) { ok = false; break; }
           tc_fence_after();
@@ -975,7 +1016,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     };
     auto row_map = [&](const Item& x) {
       RowMap m;
-      const int grow = x.pair * 2 * BM + t * BM + row;
+      const int grow = SPLIT ? row : x.pair * 2 * BM + t * BM + row;
       m.valid = grow < total_rows;
       m.r = m.valid ? grow / a.group : 0;
       m.hq = x.kvh * a.group + (m.valid ? grow % a.group : 0);
@@ -986,7 +1027,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const RowMap m = row_map(x);
       const T* qrow = static_cast<const T*>(a.q) + (long long)x.b * a.qs0 + (long long)m.hq * a.qs1 +
                       (long long)m.r * a.qs2;
-      uint8_t* qt = smem + Q2_OFF + t * kTileBytes;
+      uint8_t* qt = smem + Q2_OFF + (SPLIT ? 0 : t) * kTileBytes;
       uint4 v[16];  // all loads in flight before the first shared-memory store
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc)
@@ -994,26 +1035,27 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v[cc];
       fence_proxy_async();
-      mbar_arrive(bar(C_Q_FULL + t));
+      mbar_arrive(bar(C_Q_FULL + (SPLIT ? 0 : t)));
     };
     auto next_item = [&](int& kk, Item& nx) -> bool {
       for (;; ++kk) {
         if (!item_at(kk, nx)) return false;
-        if (t == 0 || nx.pair * 2 * BM + BM < total_rows) return true;
+        if (SPLIT || t == 0 || nx.pair * 2 * BM + BM < total_rows) return true;
       }
     };
     int sc = 0, ic = 0, k = 0;
     bool ok = true;
     Item it;
     bool have = next_item(k, it);
-    if (have) write_q(it);
+    if (have && (!SPLIT || t == 0)) write_q(it);
+    const int i_first = SPLIT ? t : 0, i_step = SPLIT ? 2 : 1;  // this warpgroup's key tiles
     while (have) {
       const int t0 = first_tile(it.b);
       const int n = n_tiles_all - t0;
       const RowMap m = row_map(it);
       const uint32_t* brow = a.bits + ((long long)it.b * a.rows + m.r) * a.row_words + t0 * 4;
       float m_run = -INFINITY, l_run = 0.f;
-      for (int i = 0; i < n; ++i) {
+      for (int i = i_first; i < n; i += i_step) {
         const uint4 w = m.valid ? *reinterpret_cast<const uint4*>(brow + i * 4) : make_uint4(0, 0, 0, 0);
         ok = mbar_wait(bar(C_S_FULL + t), sc & 1, abort_flag, a.err, 28);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
@@ -1064,7 +1106,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
           tmem_st8(s_addr + cc * 8, pk);
         }
-        if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+        if (i > i_first && __any_sync(0xffffffffu, corr != 1.f)) {
           // O_t holds tiles < i: their P.V MMAs were issued before S_t,i, and the commit
           // that signalled S_t,i covers them; P_t,i . V_i waits for P_FULL below.
 #pragma unroll
@@ -1089,12 +1131,36 @@ __global__ void __launch_bounds__(kThreads2, 1)
       Item nx;
       int kn = k + 1;
       const bool have_next = next_item(kn, nx);
-      if (have_next) write_q(nx);
+      // (SPLIT: warpgroup 1's last S may still read Q tile 0; the next Q waits for the merge)
+      if (have_next && !SPLIT) write_q(nx);
       ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      ++ic;
       tc_fence_after();
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float c0 = 1.f, c1 = 0.f;  // SPLIT: weights of O0 and O1 in the merged output
+      bool use1 = false;
+      if (SPLIT) {
+        float2* xch = reinterpret_cast<float2*>(smem + Q2_OFF + kTileBytes);  // Q tile 1 is unused
+        if (t == 1) {
+          xch[row] = make_float2(m_run, l_run);
+          mbar_arrive(bar(C_XCHG));
+          ++ic;
+          it = nx;
+          k = kn;
+          have = have_next;
+          continue;
+        }
+        ok = mbar_wait(bar(C_XCHG), ic & 1, abort_flag, a.err, 30);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const float2 ml1 = xch[row];
+        const float mm = fmaxf(m_run, ml1.x);
+        c0 = m_run == -INFINITY ? 0.f : ex2(m_run - mm);
+        use1 = ml1.x != -INFINITY;
+        c1 = use1 ? ex2(ml1.x - mm) : 0.f;
+        const float l = l_run * c0 + (use1 ? ml1.y * c1 : 0.f);
+        inv = l > 0.f ? 1.f / l : 0.f;
+      }
+      ++ic;
       T* orow = static_cast<T*>(a.out) + (((long long)it.b * a.rows + m.r) * a.q_heads + m.hq) * HD;
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -1102,6 +1168,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
         tmem_ld32(o_addr + cc * 64, o);
         tmem_ld32(o_addr + cc * 64 + 32, o + 32);
         tmem_wait_ld();
+        if (SPLIT) {
+          const uint32_t o1_addr = tmem + lane_addr + O2_COL(1) + cc * 64;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float o1[32];
+            tmem_ld32(o1_addr + h * 32, o1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[h * 32 + j] = o[h * 32 + j] * c0 + (use1 ? o1[j] * c1 : 0.f);
+          }
+        }
         if (m.valid) {
 #pragma unroll
           for (int j = 0; j < 64; j += 8) {
@@ -1115,6 +1192,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
       }
       tc_fence_before();
+      if (SPLIT && have_next) write_q(nx);  // O0 and O1 are read: the next item may start
       it = nx;
       k = kn;
       have = have_next;
@@ -1176,9 +1254,9 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <typename T>
+template <typename T, bool SPLIT>
 int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, cudaStream_t stream) {
-  auto kern = attn_pair_kernel<T>;
+  auto kern = attn_pair_kernel<T, SPLIT>;
   // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
   // per thread; any other count could leave the increase waiting for registers.
   static int regs = -1;
@@ -1242,7 +1320,10 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   s.err = err;
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
-    return bf ? launch_pair<__nv_bfloat16>(mk, mv, s, stream) : launch_pair<__half>(mk, mv, s, stream);
+    // at most one 128-row tile per (sequence, KV head): the two warpgroups split the keys
+    if ((long long)s.group * s.rows <= BM)
+      return bf ? launch_pair<__nv_bfloat16, true>(mk, mv, s, stream) : launch_pair<__half, true>(mk, mv, s, stream);
+    return bf ? launch_pair<__nv_bfloat16, false>(mk, mv, s, stream) : launch_pair<__half, false>(mk, mv, s, stream);
   }
   const int min_group = a.mask_dtype == SPECKV_F32 ? mask_min_group<float>() : mask_min_group<uint16_t>();
   if (a.mask != nullptr && s.group >= min_group) {

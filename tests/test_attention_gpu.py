@@ -127,7 +127,12 @@ def test_visibility_bits_scattered_padding():
 
 @pytest.mark.parametrize('batch,hq,hkv,rows,past,ragged', [(4, 16, 2, 61, 700, True), (3, 28, 4, 61, 300, True),
                                                           (2, 40, 8, 61, 260, True), (2, 16, 2, 17, 3000, True),
-                                                          (1, 16, 2, 1, 129, False), (5, 8, 2, 33, 127, False)])
+                                                          (1, 16, 2, 1, 129, False), (5, 8, 2, 33, 127, False),
+                                                          # at most 128 packed rows per (sequence, KV head):
+                                                          # the two warpgroups split the key tiles
+                                                          (3, 16, 2, 10, 2013, True), (2, 16, 2, 16, 100, False),
+                                                          (4, 8, 1, 16, 300, True), (2, 28, 4, 18, 500, True),
+                                                          (3, 16, 2, 5, 250, False), (70, 16, 2, 10, 700, True)])
 def test_tensor_core_bits_path_vs_oracle(batch, hq, hkv, rows, past, ragged):
     q, k, v, mask, parents, pad = random_case(batch, hq, hkv, rows, past, 128, seed=batch * 13 + hq, ragged=ragged)
     tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(parents).cuda(),
