@@ -15,7 +15,7 @@ F32, BF16, F16 = 0, 1, 2
 
 DEVICE_ERROR_KINDS = {1: 'remap index', 2: 'compact index', 3: 'move index', 4: 'tree parent index',
                       5: 'padding owner index', 6: 'wait timeout', 7: 'scheduling packet',
-                      8: 'seen index', 9: 'history index'}
+                      8: 'seen index', 9: 'history index', 10: 'row table'}
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -25,11 +25,12 @@ _pp = ctypes.POINTER(ctypes.c_void_p)
 
 # name -> argtypes (every function returns int status)
 SIGNATURES = {
-    'speckv_append_rows': [_pp, _pp, _pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _i32, _p],
+    'speckv_append_rows': [_pp, _pp, _pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _i32, _p,
+                           _i64, _p],
     'speckv_compact_suffix': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32,
-                              _p],
+                              _p, _i64, _p],
     'speckv_commit_round': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64,
-                            _p, _i64, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _p],
+                            _p, _i64, _i64, _p, _p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _p],
     'speckv_remap_rows': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i32, _p],
     'speckv_remap_rows_static': [_pp, _pp, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],
     'speckv_move_rows': [_pp, _pp, _i32, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _p],
@@ -43,7 +44,7 @@ SIGNATURES = {
     'speckv_position_update': [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p],
     'speckv_tree_mask_bits': [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p, _p],
     'speckv_tree_attention_bits': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64,
-                                   _i64, ctypes.c_float, _i32, _p],
+                                   _i64, ctypes.c_float, _i32, _p, _i64, _p],
     'speckv_tree_attention': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                               ctypes.c_float, _i32, _p],
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],

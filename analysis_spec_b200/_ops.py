@@ -39,8 +39,19 @@ def _chunks(n):
         yield start, min(n, start + _lib.MAX_LAYERS)
 
 
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True):
-    """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers).
+def _row_table(fn, row_table, batch, pool_rows):
+    """(pointer, pool rows) of an optional logical -> physical row table."""
+    if row_table is None:
+        return None, 0
+    _require_cuda(row_table)
+    if row_table.dtype != torch.long or not row_table.is_contiguous() or row_table.numel() < batch:
+        raise ValueError(f'{fn}: row table must be a contiguous int64 tensor with an entry per sequence')
+    return row_table.data_ptr(), pool_rows
+
+
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None):
+    """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers);
+    with `row_table` sequence b goes to pool row row_table[b].
 
     With ``launch=False`` the arguments are validated and marshalled now and a callable
     that issues the launches is returned, so the host work can run while the GPU is
@@ -51,8 +62,9 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=Tru
     batch, h, rows, d = k0.shape
     if h != heads or d != dim or tuple(v0.shape) != tuple(k0.shape):
         raise ValueError('appended K/V shape does not match the pool')
-    if batch > bcap:
+    if batch > bcap and row_table is None:
         raise ValueError('appended batch exceeds pool batch capacity')
+    table, table_rows = _row_table('append_rows', row_table, batch, bcap)
     if k0.stride(3) != 1 or v0.stride(3) != 1:
         raise ValueError('appended K/V need unit stride on head_dim')
     for srcs, first in ((key_srcs, k0), (value_srcs, v0)):
@@ -67,7 +79,7 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=Tru
               _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]),
               _lib.ptr_array([s.data_ptr() for s in key_srcs[a:b]]),
               _lib.ptr_array([s.data_ptr() for s in value_srcs[a:b]]),
-              b - a, batch, heads, rows, dim, capacity, length, ks, vs, es, stream)
+              b - a, batch, heads, rows, dim, capacity, length, ks, vs, es, table, table_rows, stream)
              for a, b in _chunks(len(key_pools))]
     return _issue('speckv_append_rows', calls, launch)
 
@@ -88,30 +100,33 @@ def _issue(name, calls, launch):
     return go
 
 
-def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width):
-    """Accepted-suffix compaction of every layer (one launch per 64 layers)."""
+def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width, row_table=None):
+    """Accepted-suffix compaction of every layer (one launch per 64 layers); with `row_table`
+    sequence b is pool row row_table[b]."""
     _require_cuda(key_pools[0], chosen)
     _, heads, capacity, dim = _pool_geometry(key_pools[0])
     if chosen.dtype != torch.long or chosen.dim() != 2:
         raise ValueError('chosen indices must be a (batch, width) int64 tensor')
-    if chosen.shape[0] < batch or chosen.shape[1] < width or batch > key_pools[0].shape[0]:
+    if chosen.shape[0] < batch or chosen.shape[1] < width or (batch > key_pools[0].shape[0] and row_table is None):
         raise ValueError('chosen indices do not cover the live batch / width')
+    table, table_rows = _row_table('compact_suffix', row_table, batch, key_pools[0].shape[0])
     es = key_pools[0].element_size()
     for a, b in _chunks(len(key_pools)):
         _lib.call('speckv_compact_suffix', _lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
                   _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim,
                   capacity, length, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, extension, width,
-                  es, _stream(chosen))
+                  es, table, table_rows, _stream(chosen))
 
 
 def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, newly_padded=None, positions=None,
-                 past_positions=None, pad_rows=None, owners=None, pad_live=None, launch=True):
+                 past_positions=None, pad_rows=None, owners=None, pad_live=None, launch=True, row_table=None):
     """Compaction of every layer + position/padding update of one verify round in one launch,
     with width and extension taken from the device packet (no host round trip).
 
     `chosen` / `newly_padded` / `positions` are full-width (batch, max_width) schedule outputs.
     Pass no pools to update positions only, no `positions` to compact only. With
-    ``launch=False`` returns a callable that issues the prepared launch (see append_rows).
+    ``launch=False`` returns a callable that issues the prepared launch (see append_rows);
+    with `row_table` sequence b is pool row row_table[b].
     """
     key_pools = list(key_pools or [])
     _require_cuda(packet, chosen, newly_padded, positions, past_positions, pad_rows, owners, pad_live,
@@ -147,14 +162,16 @@ def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, ne
     stream = _stream(packet)
     if not key_pools:
         return _issue('speckv_commit_round', [(None, None, 0, batch, 1, 1, 1, 0, 1, None, 0, 0, past,
-                                               packet.data_ptr(), packet.stride(0), max_width, *pos_args, stream)],
+                                               packet.data_ptr(), packet.stride(0), max_width, *pos_args, None, 0,
+                                               stream)],
                       launch)
     _, heads, capacity, dim = _pool_geometry(key_pools[0])
+    table, table_rows = _row_table('commit_round', row_table, batch, key_pools[0].shape[0])
     es = key_pools[0].element_size()
     calls = [(_lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
               _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]), b - a, batch, heads, dim, capacity,
               length, es, chosen.data_ptr(), chosen.stride(0), chosen.stride(1), past, packet.data_ptr(),
-              packet.stride(0), max_width, *(pos_args if a == 0 else no_pos), stream)
+              packet.stride(0), max_width, *(pos_args if a == 0 else no_pos), table, table_rows, stream)
              for a, b in _chunks(len(key_pools))]
     return _issue('speckv_commit_round', calls, launch)
 
@@ -376,19 +393,23 @@ def tree_mask_bits(parents, past, steps, bits, first_col, pad=None):
               bits.data_ptr(), bits.shape[2], first_col.data_ptr(), _stream(parents))
 
 
-def _check_qkv(query, key, value):
+def _check_qkv(query, key, value, any_kv_rows=False):
     if query.dtype not in _DTYPE_CODE or key.dtype != query.dtype or value.dtype != query.dtype:
         raise ValueError('query/key/value must share a float dtype')
     if query.stride(3) != 1 or key.stride(3) != 1 or value.stride(3) != 1:
         raise ValueError('query/key/value need unit stride on head_dim')
-    if tuple(value.shape) != tuple(key.shape) or key.shape[0] != query.shape[0] or key.shape[3] != query.shape[3]:
+    if tuple(value.shape) != tuple(key.shape) or key.shape[3] != query.shape[3] or \
+            (key.shape[0] != query.shape[0] and not any_kv_rows):
         raise ValueError('key/value shapes do not match the query')
 
 
-def tree_attention_bits(query, key, value, bits, first_col, scale, out=None):
-    """GQA attention with visibility from tree_mask_bits (no dense mask read)."""
-    _require_cuda(query, key, value, bits, first_col)
-    _check_qkv(query, key, value)
+def tree_attention_bits(query, key, value, bits, first_col, scale, out=None, row_table=None):
+    """GQA attention with visibility from tree_mask_bits (no dense mask read). With `row_table`
+    the K/V of sequence b are key[row_table[b]] / value[row_table[b]] (key / value then hold
+    every pool row)."""
+    _require_cuda(query, key, value, bits, first_col, row_table)
+    _check_qkv(query, key, value, any_kv_rows=row_table is not None)
+    table, kv_batch = _row_table('tree_attention_bits', row_table, query.shape[0], key.shape[0])
     batch, q_heads, rows, dim = query.shape
     kv_heads, kv_len = key.shape[1], key.shape[2]
     if bits.dtype != torch.int32 or not bits.is_contiguous() or bits.shape[:2] != (batch, rows):
@@ -398,7 +419,7 @@ def tree_attention_bits(query, key, value, bits, first_col, scale, out=None):
     _lib.call('speckv_tree_attention_bits', query.data_ptr(), _lib.i64_array(query.stride()[:3]), key.data_ptr(),
               _lib.i64_array(key.stride()[:3]), value.data_ptr(), _lib.i64_array(value.stride()[:3]),
               bits.data_ptr(), bits.shape[2], _ptr(first_col), out.data_ptr(), batch, q_heads, kv_heads, rows,
-              kv_len, dim, float(scale), _DTYPE_CODE[query.dtype], _stream(query))
+              kv_len, dim, float(scale), _DTYPE_CODE[query.dtype], table, kv_batch, _stream(query))
     return out
 
 

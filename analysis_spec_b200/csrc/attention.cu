@@ -47,6 +47,8 @@ void fill(AttnArgs& a, const void* q, const int64_t* qs, const void* k, const in
   a.bits = nullptr;
   a.row_words = 0;
   a.first_col = nullptr;
+  a.row_table = nullptr;
+  a.kv_batch = batch;
 }
 
 int launch(const AttnArgs& a, cudaStream_t s) {
@@ -81,7 +83,8 @@ extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_stride
                                           const uint32_t* bits, int64_t row_words, const int32_t* first_col,
                                           void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
                                           int64_t rows, int64_t kv_len, int64_t dim, float scale,
-                                          int32_t dtype, void* stream) {
+                                          int32_t dtype, const int64_t* row_table, int64_t kv_batch,
+                                          void* stream) {
   const char* fn = "speckv_tree_attention_bits";
   int st = check(fn, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim);
   if (st || batch == 0 || rows == 0) return st;
@@ -93,5 +96,14 @@ extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_stride
   a.bits = bits;
   a.row_words = row_words;
   a.first_col = first_col;
+  if (row_table != nullptr) {
+    if (kv_batch < 1 || kv_batch > (1 << 20))
+      return fail(SPECKV_EINVAL, "%s: row table needs the K/V row count (got %lld)", fn, (long long)kv_batch);
+    a.row_table = row_table;
+    a.kv_batch = kv_batch;
+    if (!sm100_supported(a))
+      return fail(SPECKV_ENOSUPPORT, "%s: row tables need the tensor-core path (head dim 128, bf16 / fp16, "
+                  "16-byte aligned rows)", fn);
+  }
   return launch(a, static_cast<cudaStream_t>(stream));
 }

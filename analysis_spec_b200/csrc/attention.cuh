@@ -19,6 +19,8 @@ struct AttnArgs {
   long long batch, q_heads, kv_heads, rows, kv_len, dim;
   float scale;
   int dtype, mask_dtype;
+  const int64_t* row_table;  // optional (bits path): pool row of each sequence's K/V
+  long long kv_batch;        // rows of the K/V tensors (>= batch without a table)
 };
 
 // CUDA-core path (any head dim <= 256, any dtype).

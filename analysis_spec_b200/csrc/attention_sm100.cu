@@ -82,6 +82,8 @@ struct Sm100Args {
   int batch, q_heads, kv_heads, group, rows, kv_len, mtiles;
   float scale_log2;       // softmax scale * log2(e)
   unsigned long long* err;
+  const int64_t* row_table;  // pair kernel: K/V pool row of each sequence (NULL: row b)
+  int kv_batch;              // K/V rows
 };
 
 // ---------------------------------------------------------------------------
@@ -852,19 +854,29 @@ __global__ void __launch_bounds__(kThreads2, 1)
       Item it;
       for (int k = 0; ok && item_at(k, it); ++k) {
         const int t0 = first_tile(it.b);
+        int kb = it.b;  // K/V row of the sequence: through the row table when there is one
+        if (a.row_table != nullptr) {
+          const long long p = a.row_table[it.b];
+          if (p < 0 || p >= a.kv_batch) {
+            record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
+            kb = 0;
+          } else {
+            kb = (int)p;
+          }
+        }
         for (int i = t0; i < n_tiles_all; ++i, ++cnt) {
           const int s = cnt & 1;
           if (cnt >= 2 && !mbar_wait(bar(C_K_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 21)) { ok = false; break; }
           const uint32_t kd = sbase + K2_OFF + s * kTileBytes;
           mbar_expect_tx(bar(C_K_FULL + s), kTileBytes);
-          tma_load_4d(kd, &tmk, bar(C_K_FULL + s), 0, i * BN, it.kvh, it.b);
-          tma_load_4d(kd + kTileHalf, &tmk, bar(C_K_FULL + s), 64, i * BN, it.kvh, it.b);
+          tma_load_4d(kd, &tmk, bar(C_K_FULL + s), 0, i * BN, it.kvh, kb);
+          tma_load_4d(kd + kTileHalf, &tmk, bar(C_K_FULL + s), 64, i * BN, it.kvh, kb);
           issued_k = cnt + 1;
           if (cnt >= 2 && !mbar_wait(bar(C_V_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 22)) { ok = false; break; }
           const uint32_t vd = sbase + V2_OFF + s * kTileBytes;
           mbar_expect_tx(bar(C_V_FULL + s), kTileBytes);
-          tma_load_4d(vd, &tmv, bar(C_V_FULL + s), 0, i * BN, it.kvh, it.b);
-          tma_load_4d(vd + kTileHalf, &tmv, bar(C_V_FULL + s), 64, i * BN, it.kvh, it.b);
+          tma_load_4d(vd, &tmv, bar(C_V_FULL + s), 0, i * BN, it.kvh, kb);
+          tma_load_4d(vd + kTileHalf, &tmv, bar(C_V_FULL + s), 64, i * BN, it.kvh, kb);
           issued_v = cnt + 1;
         }
       }
@@ -1293,8 +1305,8 @@ bool sm100_supported(const AttnArgs& a) {
 int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   const uint32_t* bits = a.bits;
   CUtensorMap mk, mv;
-  if (!make_kv_map(&mk, a.k, a.ks, a.batch, a.kv_heads, a.kv_len, a.dtype) ||
-      !make_kv_map(&mv, a.v, a.vs, a.batch, a.kv_heads, a.kv_len, a.dtype))
+  if (!make_kv_map(&mk, a.k, a.ks, a.kv_batch, a.kv_heads, a.kv_len, a.dtype) ||
+      !make_kv_map(&mv, a.v, a.vs, a.kv_batch, a.kv_heads, a.kv_len, a.dtype))
     return fail(SPECKV_ECUDA, "speckv_tree_attention: cuTensorMapEncodeTiled failed");
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "speckv_tree_attention: device error word unavailable");
@@ -1318,6 +1330,8 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   s.mtiles = (int)((s.group * a.rows + BM - 1) / BM);
   s.scale_log2 = a.scale * 1.4426950408889634f;
   s.err = err;
+  s.row_table = a.row_table;
+  s.kv_batch = (int)a.kv_batch;
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
     // at most one 128-row tile per (sequence, KV head): the two warpgroups split the keys

@@ -24,6 +24,23 @@ struct SrcTable {
   const char* ptr[2 * SPECKV_MAX_LAYERS];
 };
 
+// Optional logical -> physical pool row table: logical sequence b lives in pool row map[b]
+// (NULL: row b). An entry outside [0, rows) is reported in the device error word and that
+// sequence is skipped, so a bad table never addresses memory outside the pools.
+struct RowTable {
+  const int64_t* map;
+  long long rows;
+};
+__device__ __forceinline__ long long phys_row(const RowTable& t, long long b, unsigned long long* err) {
+  if (t.map == nullptr) return b;
+  const long long p = t.map[b];
+  if (p < 0 || p >= t.rows) {
+    record_error(err, SPECKV_DERR_ROW_TABLE, p);
+    return -1;
+  }
+  return p;
+}
+
 template <int V>
 __device__ __forceinline__ typename Vec<V>::T load_vec(const char* p) {
   return *reinterpret_cast<const typename Vec<V>::T*>(p);
@@ -43,6 +60,8 @@ struct AppendGeom {
   long long dst_sb, dst_sh, dst_t0, row_bytes;
   long long src_sb[2], src_sh[2], src_st[2];  // byte strides of the K / V source
   uint32_t total;                             // vectors per tensor
+  RowTable rt;                                // destination pool row of each sequence
+  unsigned long long* err;
 };
 
 template <int V, int UNROLL>
@@ -64,11 +83,14 @@ __global__ void __launch_bounds__(kThreads) append_kernel(PoolTable dst, SrcTabl
       g.nvec.divmod(i, row, lane);
       g.rows.divmod(row, bh, t);
       g.heads.divmod(bh, b, h);
-      const long long so = (long long)b * g.src_sb[kv] + (long long)h * g.src_sh[kv] +
-                           (long long)t * g.src_st[kv] + (long long)lane * V;
-      buf[u] = load_vec<V>(s + so);
-      doff[u] = (long long)b * g.dst_sb + (long long)h * g.dst_sh + g.dst_t0 +
-                (long long)t * g.row_bytes + (long long)lane * V;
+      const long long pb = phys_row(g.rt, b, g.err);
+      if (pb >= 0) {
+        const long long so = (long long)b * g.src_sb[kv] + (long long)h * g.src_sh[kv] +
+                             (long long)t * g.src_st[kv] + (long long)lane * V;
+        buf[u] = load_vec<V>(s + so);
+        doff[u] = pb * g.dst_sb + (long long)h * g.dst_sh + g.dst_t0 + (long long)t * g.row_bytes +
+                  (long long)lane * V;
+      }
     }
   }
 #pragma unroll
@@ -90,6 +112,7 @@ struct CompactGeom {
   long long csb, csw;  // chosen strides (elements)
   uint32_t n;          // rows per group (width - extension)
   uint32_t groups;     // 2 * layers * batch * heads
+  RowTable rt;         // pool row of each sequence
 };
 
 template <int V, int MAXR>
@@ -102,7 +125,9 @@ __global__ void __launch_bounds__(kThreads) compact_warp_kernel(PoolTable pools,
   uint32_t tensor, bh, b, h;
   g.bh.divmod(group, tensor, bh);
   g.heads.divmod(bh, b, h);
-  char* base = pools.ptr[tensor] + (long long)b * g.sb + (long long)h * g.sh;
+  const long long pb = phys_row(g.rt, b, err);
+  if (pb < 0) return;  // the whole warp shares b
+  char* base = pools.ptr[tensor] + pb * g.sb + (long long)h * g.sh;
   const uint32_t nv = g.n * g.nvec.d;
   T buf[MAXR];
   long long src[MAXR];
@@ -146,7 +171,9 @@ __global__ void __launch_bounds__(kThreads) compact_smem_kernel(PoolTable pools,
   uint32_t tensor, bh, b, h;
   g.bh.divmod(group, tensor, bh);
   g.heads.divmod(bh, b, h);
-  char* base = pools.ptr[tensor] + (long long)b * g.sb + (long long)h * g.sh;
+  const long long pb = phys_row(g.rt, b, err);
+  if (pb < 0) return;  // the whole CTA shares b
+  char* base = pools.ptr[tensor] + pb * g.sb + (long long)h * g.sh;
   const uint32_t nv = g.n * g.nvec.d;
   for (uint32_t i = threadIdx.x; i < nv; i += kThreads) {
     uint32_t j, lv;
@@ -372,7 +399,9 @@ __global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools,
   uint32_t tensor, bh, b, h;
   g.c.bh.divmod(group, tensor, bh);
   g.c.heads.divmod(bh, b, h);
-  char* base = pools.ptr[tensor] + (long long)b * g.c.sb + (long long)h * g.c.sh;
+  const long long pb = phys_row(g.c.rt, b, err);
+  if (pb < 0) return;  // the whole warp shares b
+  char* base = pools.ptr[tensor] + pb * g.c.sb + (long long)h * g.c.sh;
   const uint32_t nv = (uint32_t)(width - ext) * g.c.nvec.d;
   T buf[MAXR];
   int src[MAXR];  // source position, -1 = skipped (length < 2^31 is checked on the host)
@@ -481,14 +510,25 @@ struct CommitPlan final : LaunchPlan {
 int prepare_append(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
                    const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                    int64_t dim, int64_t capacity, int64_t length, const int64_t* key_src_strides,
-                   const int64_t* value_src_strides, int32_t elem_bytes, LaunchPlan** out);
+                   const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* row_table,
+                   int64_t pool_rows, LaunchPlan** out);
 int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t layers, int64_t batch, int64_t heads,
                    int64_t dim, int64_t capacity, int64_t length, int32_t elem_bytes, const int64_t* chosen,
                    int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, const int64_t* packet,
                    int64_t packet_stride, int64_t max_width, uint8_t* pad_rows, int64_t pad_rows_stride,
                    int64_t pad_rows_count, const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
                    const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
-                   int64_t positions_stride_b, int64_t* past_positions, LaunchPlan** out);
+                   int64_t positions_stride_b, int64_t* past_positions, const int64_t* row_table,
+                   int64_t pool_rows, LaunchPlan** out);
+
+// A row table needs the pools' row count to bound its entries.
+int check_table(const char* fn, const int64_t* row_table, int64_t pool_rows, int64_t batch) {
+  if (row_table != nullptr && pool_rows < 1)
+    return fail(SPECKV_EINVAL, "%s: a row table needs the pools' row count", fn);
+  if (row_table == nullptr && pool_rows != 0 && pool_rows < batch)
+    return fail(SPECKV_EINVAL, "%s: %lld pool rows for %lld sequences", fn, (long long)pool_rows, (long long)batch);
+  return SPECKV_OK;
+}
 
 // Runs a prepared plan once and frees it.
 int launch_once(int st, LaunchPlan* plan, void* stream) {
@@ -508,10 +548,11 @@ extern "C" int speckv_append_rows(void* const* key_pools, void* const* value_poo
                                   int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                                   int64_t dim, int64_t capacity, int64_t length,
                                   const int64_t* key_src_strides, const int64_t* value_src_strides,
-                                  int32_t elem_bytes, void* stream) {
+                                  int32_t elem_bytes, const int64_t* row_table, int64_t pool_rows, void* stream) {
   LaunchPlan* plan = nullptr;
   const int st = prepare_append(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
-                                capacity, length, key_src_strides, value_src_strides, elem_bytes, &plan);
+                                capacity, length, key_src_strides, value_src_strides, elem_bytes, row_table,
+                                pool_rows, &plan);
   return launch_once(st, plan, stream);
 }
 
@@ -520,11 +561,13 @@ extern "C" int speckv_append_rows_prepare(void* const* key_pools, void* const* v
                                           int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                                           int64_t dim, int64_t capacity, int64_t length,
                                           const int64_t* key_src_strides, const int64_t* value_src_strides,
-                                          int32_t elem_bytes, void** plan) {
+                                          int32_t elem_bytes, const int64_t* row_table, int64_t pool_rows,
+                                          void** plan) {
   if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_append_rows_prepare: null plan");
   LaunchPlan* p = nullptr;
   const int st = prepare_append(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
-                                capacity, length, key_src_strides, value_src_strides, elem_bytes, &p);
+                                capacity, length, key_src_strides, value_src_strides, elem_bytes, row_table,
+                                pool_rows, &p);
   *plan = st ? nullptr : p;
   return st;
 }
@@ -542,9 +585,11 @@ int prepare_append(void* const* key_pools, void* const* value_pools, const void*
                            const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads,
                            int64_t rows, int64_t dim, int64_t capacity, int64_t length,
                            const int64_t* key_src_strides, const int64_t* value_src_strides, int32_t elem_bytes,
-                           LaunchPlan** out) {
+                           const int64_t* row_table, int64_t pool_rows, LaunchPlan** out) {
   const char* fn = "speckv_append_rows";
   int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
+  if (st) return st;
+  st = check_table(fn, row_table, pool_rows, batch);
   if (st) return st;
   if (key_srcs == nullptr || value_srcs == nullptr || key_src_strides == nullptr || value_src_strides == nullptr)
     return fail(SPECKV_EINVAL, "%s: null source table or strides", fn);
@@ -597,6 +642,15 @@ int prepare_append(void* const* key_pools, void* const* value_pools, const void*
     g.src_st[kv] = s[2] * elem_bytes;
   }
   g.total = (uint32_t)total;
+  g.rt = RowTable{row_table, pool_rows};
+  g.err = nullptr;
+  if (row_table != nullptr) {
+    g.err = device_error_word();
+    if (g.err == nullptr) {
+      delete plan;
+      return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
+    }
+  }
   constexpr int UNROLL = 4;
   plan->src = src;
   plan->vec = vec;
@@ -611,9 +665,12 @@ extern "C" int speckv_compact_suffix(void* const* key_pools, void* const* value_
                                      int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
                                      int64_t length, const int64_t* chosen, int64_t chosen_stride_b,
                                      int64_t chosen_stride_w, int64_t past, int64_t extension,
-                                     int64_t width, int32_t elem_bytes, void* stream) {
+                                     int64_t width, int32_t elem_bytes, const int64_t* row_table,
+                                     int64_t pool_rows, void* stream) {
   const char* fn = "speckv_compact_suffix";
   int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
+  if (st) return st;
+  st = check_table(fn, row_table, pool_rows, batch);
   if (st) return st;
   if (batch < 0 || past < 0 || extension < 0 || width < 0 || length < 0)
     return fail(SPECKV_EINVAL, "%s: negative size", fn);
@@ -646,6 +703,7 @@ extern "C" int speckv_compact_suffix(void* const* key_pools, void* const* value_
   g.csw = chosen_stride_w;
   g.n = (uint32_t)n;
   g.groups = (uint32_t)groups;
+  g.rt = RowTable{row_table, pool_rows};
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -673,12 +731,14 @@ extern "C" int speckv_commit_round(void* const* key_pools, void* const* value_po
                                    int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
                                    uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
                                    int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
-                                   int64_t* past_positions, void* stream) {
+                                   int64_t* past_positions, const int64_t* row_table, int64_t pool_rows,
+                                   void* stream) {
   LaunchPlan* plan = nullptr;
   const int st = prepare_commit(key_pools, value_pools, layers, batch, heads, dim, capacity, length, elem_bytes,
                                 chosen, chosen_stride_b, chosen_stride_w, past, packet, packet_stride, max_width,
                                 pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
-                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, &plan);
+                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, row_table,
+                                pool_rows, &plan);
   return launch_once(st, plan, stream);
 }
 
@@ -690,13 +750,15 @@ extern "C" int speckv_commit_round_prepare(void* const* key_pools, void* const* 
                                            uint8_t* pad_rows, int64_t pad_rows_stride, int64_t pad_rows_count,
                                            const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
                                            const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
-                                           int64_t positions_stride_b, int64_t* past_positions, void** plan) {
+                                           int64_t positions_stride_b, int64_t* past_positions,
+                                           const int64_t* row_table, int64_t pool_rows, void** plan) {
   if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_commit_round_prepare: null plan");
   LaunchPlan* p = nullptr;
   const int st = prepare_commit(key_pools, value_pools, layers, batch, heads, dim, capacity, length, elem_bytes,
                                 chosen, chosen_stride_b, chosen_stride_w, past, packet, packet_stride, max_width,
                                 pad_rows, pad_rows_stride, pad_rows_count, owners, pad_live, pad_live_stride,
-                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, &p);
+                                newly_padded, np_stride_b, positions, positions_stride_b, past_positions, row_table,
+                                pool_rows, &p);
   *plan = st ? nullptr : p;
   return st;
 }
@@ -710,10 +772,13 @@ int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t lay
                            int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
                            uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
                            int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
-                           int64_t* past_positions, LaunchPlan** out) {
+                           int64_t* past_positions, const int64_t* row_table, int64_t pool_rows,
+                           LaunchPlan** out) {
   const char* fn = "speckv_commit_round";
   if (layers != 0) {
     int st = check_common(fn, key_pools, value_pools, layers, heads, dim, capacity, elem_bytes);
+    if (st) return st;
+    st = check_table(fn, row_table, pool_rows, batch);
     if (st) return st;
   }
   if (batch < 0 || past < 0 || max_width < 1 || length < 0) return fail(SPECKV_EINVAL, "%s: bad sizes", fn);
@@ -765,6 +830,7 @@ int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t lay
   g.c.csw = chosen_stride_w;
   g.c.n = 0;
   g.c.groups = (uint32_t)groups;
+  g.c.rt = RowTable{layers != 0 ? row_table : nullptr, pool_rows};
   g.chosen = chosen;
   g.packet = packet;
   g.ps = packet_stride;

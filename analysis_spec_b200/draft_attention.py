@@ -40,6 +40,9 @@ def draft_sdpa(query_states, key_states, value_states, attention_mask, num_key_v
         vis = dense_mask_visibility(attention_mask, mask, batch, rows, kv_len)
         if vis is not None:
             return _ops.tree_attention_bits(query_states, key_states, value_states, vis.bits, vis.first_col,
-                                            scale).transpose(1, 2)
+                                            scale, row_table=getattr(key_states, '_speckv_rows', None)
+                                            ).transpose(1, 2)
+    if getattr(key_states, '_speckv_rows', None) is not None:
+        raise ValueError('K/V of a row-table cache need a 0 / lowest-valued mask, head dim 128 and bf16 / fp16')
     out = _ops.tree_attention(query_states, key_states, value_states, mask, scale)
     return out.transpose(1, 2)

@@ -10,6 +10,15 @@ All row movement runs in libspeckv's sm_100a kernels. Cache-wide operations
 ``commit_accepted``) move every layer, K and V, in ONE launch instead of the
 reference's per-layer launches.
 
+Row tables (``OPDStaticCache(..., row_table=True)``; the reference has none): sequence b
+lives in pool row ``row_table[b]`` instead of row b. Releasing finished sequences
+(``swap_remove``) and admitting new ones (``admit``) then rewrite the table instead of
+moving whole histories; append, commit and the tree-verify attention read through it.
+The per-layer views handed to the attention are then the pools' full row range tagged
+with the table (``_speckv_rows``), which this package's attention functions follow; an
+attention implementation that ignores the tag would read the wrong rows, so the mode is
+for callers that run ``tree_attention`` / ``draft_attention``.
+
 Reference semantics followed (file:line in the reference project):
   StaticAppendLayer            helper/opd_static_cache.py:17-174
   OPDStaticCache               helper/opd_static_cache.py:177-244
@@ -54,9 +63,23 @@ class StaticAppendLayer(CacheLayerMixin):
     def owner(self):
         return self._owner_ref() if self._owner_ref is not None else None
 
+    def _table(self):
+        owner = self.owner
+        return owner._device_rows(self.batch_size) if owner is not None and owner.uses_row_table else None
+
+    def _view(self, pool):
+        if pool is None:
+            return None
+        table = self._table()
+        if table is None:
+            return pool[:self.batch_size, :, :self.length, :]
+        view = pool[:, :, :self.length, :]
+        view._speckv_rows = table  # sequence b is pool row table[b]
+        return view
+
     @property
     def keys(self):
-        return None if self.key_pool is None else self.key_pool[:self.batch_size, :, :self.length, :]
+        return self._view(self.key_pool)
 
     @keys.setter
     def keys(self, value):
@@ -65,7 +88,7 @@ class StaticAppendLayer(CacheLayerMixin):
 
     @property
     def values(self):
-        return None if self.value_pool is None else self.value_pool[:self.batch_size, :, :self.length, :]
+        return self._view(self.value_pool)
 
     @values.setter
     def values(self, value):
@@ -79,7 +102,9 @@ class StaticAppendLayer(CacheLayerMixin):
             raise RuntimeError('cache assignment before initialization')
         if view.untyped_storage().data_ptr() != pool.untyped_storage().data_ptr():
             raise RuntimeError('use batch_select_indices for row remap; external KV replacement is unsupported')
-        self.length, self.batch_size = view.shape[-2], view.shape[0]
+        self.length = view.shape[-2]
+        if self._table() is None:
+            self.batch_size = view.shape[0]
 
     # ---- allocation ----------------------------------------------------------
     def _chunk(self):
@@ -115,9 +140,12 @@ class StaticAppendLayer(CacheLayerMixin):
         rows = max(batch_needed, self.batch_capacity)
         shape = (rows, self.key_pool.shape[1], capacity, self.key_pool.shape[-1])
         old_keys, old_values = self.keys, self.values
+        if self._table() is not None:  # rows are scattered: keep every row in place
+            old_keys = self.key_pool[:, :, :self.length]
+            old_values = self.value_pool[:, :, :self.length]
         keys = torch.empty(shape, dtype=self.key_pool.dtype, device=self.key_pool.device)
         values = torch.empty(shape, dtype=self.value_pool.dtype, device=self.value_pool.device)
-        if self.length and self.batch_size:
+        if self.length and old_keys.shape[0]:
             _ops.append_rows([keys], [values], [old_keys], [old_values], 0)
         self.stats['pool_allocations'] += 1
         self.stats['full_kv_reallocations'] += 1
@@ -127,6 +155,9 @@ class StaticAppendLayer(CacheLayerMixin):
                                                       old_values.numel() * old_values.element_size())
         self.key_pool, self.value_pool = keys, values
         self.capacity, self.batch_capacity = capacity, rows
+        owner = self.owner
+        if owner is not None and owner.uses_row_table:
+            owner._fit_rows(rows)
 
     # ---- append ----------------------------------------------------------------
     def _prepare_append(self, key_states, value_states):
@@ -144,7 +175,8 @@ class StaticAppendLayer(CacheLayerMixin):
 
     def update(self, key_states, value_states, *args, **kwargs):
         key_states, value_states, end = self._prepare_append(key_states, value_states)
-        _ops.append_rows([self.key_pool], [self.value_pool], [key_states], [value_states], self.length)
+        _ops.append_rows([self.key_pool], [self.value_pool], [key_states], [value_states], self.length,
+                         row_table=self._table())
         self.length = end
         return self.keys, self.values
 
@@ -194,6 +226,8 @@ class StaticAppendLayer(CacheLayerMixin):
         return scratch
 
     def batch_select_indices(self, indices):
+        if self._table() is not None:
+            raise RuntimeError('with a row table, remap rows through the cache (OPDStaticCache.batch_select_indices)')
         new_batch = indices.numel()
         self._grow(self.length, new_batch)
         _ops.remap_rows([self.key_pool], [self.value_pool], indices, self.length, self._remap_scratch(new_batch))
@@ -217,6 +251,8 @@ class StaticAppendLayer(CacheLayerMixin):
 
     def swap_remove(self, new_batch, sources, destinations):
         """Moves disjoint live tail rows into holes below new_batch; survivors stay put."""
+        if self._table() is not None:
+            raise RuntimeError('with a row table, release rows through the cache (OPDStaticCache.swap_remove)')
         count = sources.numel()
         if count and self.length:
             _ops.move_rows([self.key_pool], [self.value_pool], sources, destinations, self.length)
@@ -235,7 +271,7 @@ class LayerViews:
     __slots__ = ('_items',)
 
     def __init__(self, layers):
-        self._items = [(l.key_pool, l.value_pool, l.batch_size, l.length) for l in layers]
+        self._items = [(l.key_pool, l.value_pool, l.batch_size, l.length, l._table()) for l in layers]
 
     def __len__(self):
         return len(self._items)
@@ -243,8 +279,12 @@ class LayerViews:
     def __getitem__(self, index):
         if isinstance(index, slice):
             return [self[i] for i in range(*index.indices(len(self._items)))]
-        k, v, b, n = self._items[index]
-        return k[:b, :, :n, :], v[:b, :, :n, :]
+        k, v, b, n, table = self._items[index]
+        if table is None:
+            return k[:b, :, :n, :], v[:b, :, :n, :]
+        k, v = k[:, :, :n, :], v[:, :, :n, :]
+        k._speckv_rows = v._speckv_rows = table
+        return k, v
 
     def __iter__(self):
         for i in range(len(self._items)):
@@ -262,9 +302,14 @@ def _uniform(layers):
 class OPDStaticCache(Cache):
     """HF ``Cache`` whose layers are StaticAppendLayer pools kept across rollouts."""
 
-    def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256):
+    def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256, row_table=False):
         if capacity < 1 or chunk_size < 1 or batch_capacity < 0:
             raise ValueError('positive KV capacity/chunk and nonnegative batch capacity required')
+        self.uses_row_table = bool(row_table)
+        # host copy of the table: a permutation of the pool rows, live sequences first
+        # (entry b < batch is sequence b's row), the rows free for admission after them
+        self._rows = []
+        self._rows_dev = None
         try:
             super().__init__(layers=[])
         except TypeError:
@@ -273,6 +318,45 @@ class OPDStaticCache(Cache):
         self.capacity, self.batch_capacity, self.chunk_size = capacity, batch_capacity, chunk_size
         self._scratch = {}
         self.kv_rows_moved = 0
+
+    # ---- row table -----------------------------------------------------------
+    def _fit_rows(self, rows):
+        """Extends the table to `rows` pool rows (the new rows are free)."""
+        if self._rows and rows > len(self._rows):
+            self._rows.extend(range(len(self._rows), rows))
+            self._upload_rows()
+
+    def _reset_rows(self, rows):
+        self._rows = list(range(rows))
+        self._upload_rows()
+
+    def _upload_rows(self):
+        layer = next((l for l in self.layers if l.key_pool is not None), None)
+        if layer is None or not self._rows:
+            return
+        staged = torch.tensor(self._rows, dtype=torch.long).pin_memory()
+        if self._rows_dev is None or self._rows_dev.numel() < len(self._rows) or \
+                self._rows_dev.device != layer.key_pool.device:
+            self._rows_dev = torch.empty(max(len(self._rows), layer.batch_capacity), dtype=torch.long,
+                                         device=layer.key_pool.device)
+        self._rows_dev[:len(self._rows)].copy_(staged, non_blocking=True)
+
+    def _device_rows(self, batch):
+        if not self._rows and batch:
+            first = next((l for l in self.layers if l.key_pool is not None), None)
+            if first is None:
+                return None
+            self._reset_rows(first.batch_capacity)
+        if self._rows_dev is None or len(self._rows) < batch:
+            raise RuntimeError('row table shorter than the live batch')
+        return self._rows_dev[:batch]
+
+    @property
+    def row_table(self):
+        """Pool row of each live sequence (host list), or None without a row table."""
+        if not self.uses_row_table or not self.layers:
+            return None
+        return list(self._rows[:self.layers[0].batch_size])
 
     # ---- rollout lifetime ------------------------------------------------------
     def begin_rollout(self, batch, batch_capacity):
@@ -283,6 +367,8 @@ class OPDStaticCache(Cache):
             layer.batch_size = batch
             for key in layer.stats:
                 layer.stats[key] = 0
+        if self.uses_row_table and self.layers and self.layers[0].key_pool is not None:
+            self._reset_rows(self.layers[0].batch_capacity)
 
     def end_rollout(self, max_retained_tokens=0):
         for layer in self.layers:
@@ -342,6 +428,9 @@ class OPDStaticCache(Cache):
         layers = self.layers
         if not layers:
             return
+        if self.uses_row_table and layers[0].key_pool is not None:
+            # through the table to pool rows, written to rows [0, new_batch): the table is identity after
+            indices = self._device_rows(layers[0].batch_size)[indices]
         new_batch = indices.numel()
         for layer in layers:
             layer._grow(layer.length, new_batch)
@@ -356,6 +445,8 @@ class OPDStaticCache(Cache):
                 _ops.remap_rows([layer.key_pool], [layer.value_pool], indices, layer.length,
                                 layer._remap_scratch(new_batch))
                 layer._count_select(new_batch)
+        if self.uses_row_table:
+            self._reset_rows(layers[0].batch_capacity)
 
     def batch_repeat_interleave(self, repeats):
         if repeats < 1:
@@ -371,6 +462,9 @@ class OPDStaticCache(Cache):
 
     def swap_remove(self, new_batch, sources, destinations):
         layers = self.layers
+        if self.uses_row_table and layers and layers[0].key_pool is not None:
+            self._swap_remove_rows(new_batch, sources, destinations)
+            return
         count = sources.numel()
         if layers and count:
             live = [l for l in layers if l.length]
@@ -383,6 +477,18 @@ class OPDStaticCache(Cache):
         for layer in layers:
             layer._count_swap(new_batch, count)
         self.kv_rows_moved += count
+
+    def _swap_remove_rows(self, new_batch, sources, destinations):
+        """swap_remove through the row table: sequence d takes sequence s's pool row for each
+        (s, d) pair and the released rows join the free tail; no KV byte moves."""
+        sources = sources.tolist() if isinstance(sources, torch.Tensor) else list(sources)
+        destinations = destinations.tolist() if isinstance(destinations, torch.Tensor) else list(destinations)
+        self._device_rows(self.layers[0].batch_size)  # table initialised
+        self._rows = release_rows(self._rows, new_batch, sources, destinations)
+        self._upload_rows()
+        for layer in self.layers:
+            layer.stats['row_compactions'] += 1
+            layer.batch_size = new_batch
 
     # ---- B200 additions ----------------------------------------------------------
     def admit(self, key_states, value_states):
@@ -407,7 +513,13 @@ class OPDStaticCache(Cache):
         start = layers[0].batch_size
         for layer in layers:
             layer._grow(max(length, 1), batch_needed=start + count)
-        if length:
+        if self.uses_row_table:
+            # the new sequences take the free rows at the table's positions [start, start + count)
+            table = self._device_rows(start + count)[start:]
+            if length:
+                _ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers], list(key_states),
+                                 list(value_states), 0, row_table=table)
+        elif length:
             _ops.append_rows([l.key_pool[start:] for l in layers], [l.value_pool[start:] for l in layers],
                              list(key_states), list(value_states), 0)
         for layer in layers:
@@ -428,12 +540,14 @@ class OPDStaticCache(Cache):
         for idx, (k, v) in enumerate(zip(key_states, value_states)):
             prepared.append(self._layer(idx)._prepare_append(k, v))
         layers = self.layers[:len(prepared)]
+        table = layers[0]._table() if layers else None
         if _uniform(layers):
             launches = [_ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers],
                                          [p[0] for p in prepared], [p[1] for p in prepared], layers[0].length,
-                                         launch=False)]
+                                         launch=False, row_table=table)]
         else:
-            launches = [_ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length, launch=False)
+            launches = [_ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length, launch=False,
+                                         row_table=table)
                         for layer, (k, v, _) in zip(layers, prepared)]
 
         def launch():
@@ -454,14 +568,15 @@ class OPDStaticCache(Cache):
         width = chosen.shape[1]
         layers = self.layers
         if layers and extension != width:
+            table = layers[0]._table()
             if _uniform(layers):
                 first = layers[0]
                 _ops.compact_suffix([l.key_pool for l in layers], [l.value_pool for l in layers],
-                                    first.batch_size, first.length, chosen, past, extension, width)
+                                    first.batch_size, first.length, chosen, past, extension, width, row_table=table)
             else:
                 for layer in layers:
                     _ops.compact_suffix([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length,
-                                        chosen, past, extension, width)
+                                        chosen, past, extension, width, row_table=table)
         self.crop(past + width)
 
     def commit_scheduled(self, chosen, past, packet, newly_padded=None, positions=None, past_positions=None,
@@ -483,10 +598,13 @@ class OPDStaticCache(Cache):
         elif _uniform(layers):
             first = layers[0]
             launches = [_ops.commit_round([l.key_pool for l in layers], [l.value_pool for l in layers],
-                                          first.batch_size, first.length, chosen, past, packet, **pos, launch=False)]
+                                          first.batch_size, first.length, chosen, past, packet, **pos, launch=False,
+                                          row_table=first._table())]
         else:
+            table = layers[0]._table()
             launches = [_ops.commit_round([layer.key_pool], [layer.value_pool], layer.batch_size, layer.length,
-                                          chosen, past, packet, **(pos if i == 0 else {}), launch=False)
+                                          chosen, past, packet, **(pos if i == 0 else {}), launch=False,
+                                          row_table=table)
                         for i, layer in enumerate(layers)]
 
         def launch():
@@ -503,6 +621,22 @@ class OPDStaticCache(Cache):
         totals['kv_rows_moved'] = self.kv_rows_moved
         totals['kv_history_copy_bytes'] = totals['full_history_copy_bytes']
         return totals
+
+
+def release_rows(rows, new_batch, sources, destinations):
+    """Row-table form of swap_remove: `rows` is the table (pool row of each sequence, then the
+    free rows). Sequence d < new_batch takes the pool row of sequence s >= new_batch for each
+    (s, d) pair, the other sequences below new_batch keep theirs, and every pool row no
+    longer referenced joins the free tail. Returns the new table (a permutation of `rows`)."""
+    if len(sources) != len(destinations):
+        raise ValueError('swap_remove needs one destination per source')
+    live = list(rows[:new_batch])
+    for src, dst in zip(sources, destinations):
+        if not (0 <= dst < new_batch <= src < len(rows)):
+            raise ValueError('swap_remove moves rows from the tail into holes below the new batch')
+        live[dst] = rows[src]
+    kept = set(live)
+    return live + [r for r in rows if r not in kept]
 
 
 def swap_remove_plan(finished):

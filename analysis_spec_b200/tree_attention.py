@@ -57,10 +57,12 @@ def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0
     if dropout:
         raise ValueError('tree_verify_attention is an inference kernel (dropout must be 0)')
     scale = scaling if scaling is not None else query.shape[-1] ** -0.5
+    rows_table = getattr(key, '_speckv_rows', None)  # K/V of a row-table cache: every pool row
     vis = attention_mask if hasattr(attention_mask, 'first_col') else getattr(attention_mask, '_speckv_visibility',
                                                                             None)
     if vis is not None and key.shape[-2] == vis.past + vis.rows and query.shape[2] == vis.rows:
-        return _ops.tree_attention_bits(query, key, value, vis.bits, vis.first_col, scale), None
+        return _ops.tree_attention_bits(query, key, value, vis.bits, vis.first_col, scale,
+                                        row_table=rows_table), None
     mask = attention_mask
     if mask is not None and mask.shape[-1] > key.shape[-2]:
         mask = mask[:, :, :, :key.shape[-2]]
@@ -72,7 +74,11 @@ def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0
         batch, rows, kv_len = query.shape[0], query.shape[2], key.shape[-2]
         dense = dense_mask_visibility(attention_mask, mask, batch, rows, kv_len)
         if dense is not None:
-            return _ops.tree_attention_bits(query, key, value, dense.bits, dense.first_col, scale), None
+            return _ops.tree_attention_bits(query, key, value, dense.bits, dense.first_col, scale,
+                                            row_table=rows_table), None
+    if rows_table is not None:
+        raise ValueError('K/V of a row-table cache need a 0 / lowest-valued mask (the visibility-bits kernel), '
+                         'head dim 128 and bf16 / fp16')
     return _ops.tree_attention(query, key, value, mask, scale), None
 
 

@@ -46,6 +46,7 @@ extern "C" {
 #define SPECKV_DERR_PACKET 7   /* scheduling packet inconsistent with the commit; value = its width */
 #define SPECKV_DERR_SEEN_INDEX 8 /* draft expansion: seen position outside [0, columns) */
 #define SPECKV_DERR_HISTORY_INDEX 9 /* history append: owner row or source position out of range */
+#define SPECKV_DERR_ROW_TABLE 10    /* row table entry outside the pools' rows; value = the entry */
 
 #define SPECKV_HISTORY_MAX_FIELDS 4
 
@@ -66,6 +67,18 @@ const char* speckv_last_error(void);
  * clear it. Synchronises `stream`. */
 int speckv_device_error(uint64_t* word, void* stream);
 
+/* ---- Row tables ------------------------------------------------------------
+ * speckv_append_rows, speckv_compact_suffix, speckv_commit_round (and their
+ * prepared forms) and speckv_tree_attention_bits take an optional row table:
+ * row_table[b] (int64, device) is the pool row holding sequence b, for b < batch;
+ * pool_rows (kv_batch for the attention) is the pools' row count, which every
+ * entry must stay below (an entry outside it sets device error
+ * SPECKV_DERR_ROW_TABLE and that sequence is skipped). NULL keeps sequence b in
+ * pool row b (pool_rows may then be 0). With a table, releasing and admitting
+ * sequences is an update of the table instead of a move of their histories
+ * (the reference's swap_remove moves whole rows, helper/opd_static_cache.py:157-174);
+ * the reference has no such table. */
+
 /* ---- KV rows: append / grow --------------------------------------------- */
 
 /* Append `rows` new positions for every (sequence, head) of `layers` layers:
@@ -80,7 +93,7 @@ int speckv_append_rows(void* const* key_pools, void* const* value_pools,
                        int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                        int64_t dim, int64_t capacity, int64_t length,
                        const int64_t* key_src_strides, const int64_t* value_src_strides,
-                       int32_t elem_bytes, void* stream);
+                       int32_t elem_bytes, const int64_t* row_table, int64_t pool_rows, void* stream);
 
 /* ---- KV rows: accepted-suffix compaction ------------------------------- */
 
@@ -96,7 +109,8 @@ int speckv_compact_suffix(void* const* key_pools, void* const* value_pools, int3
                           int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
                           int64_t length, const int64_t* chosen, int64_t chosen_stride_b,
                           int64_t chosen_stride_w, int64_t past, int64_t extension,
-                          int64_t width, int32_t elem_bytes, void* stream);
+                          int64_t width, int32_t elem_bytes, const int64_t* row_table, int64_t pool_rows,
+                          void* stream);
 
 /* ---- KV rows: device-scheduled commit of a verify round ----------------- */
 
@@ -122,7 +136,7 @@ int speckv_commit_round(void* const* key_pools, void* const* value_pools, int32_
                         int64_t pad_rows_stride, int64_t pad_rows_count, const int64_t* owners,
                         uint8_t* pad_live, int64_t pad_live_stride, const uint8_t* newly_padded,
                         int64_t np_stride_b, int64_t* positions, int64_t positions_stride_b,
-                        int64_t* past_positions, void* stream);
+                        int64_t* past_positions, const int64_t* row_table, int64_t pool_rows, void* stream);
 
 /* ---- Draft-model attention masks ---------------------------------------- */
 
@@ -204,7 +218,8 @@ int speckv_append_rows_prepare(void* const* key_pools, void* const* value_pools,
                                int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                                int64_t dim, int64_t capacity, int64_t length,
                                const int64_t* key_src_strides, const int64_t* value_src_strides,
-                               int32_t elem_bytes, void** plan);
+                               int32_t elem_bytes, const int64_t* row_table, int64_t pool_rows,
+                               void** plan);
 int speckv_commit_round_prepare(void* const* key_pools, void* const* value_pools, int32_t layers,
                                 int64_t batch, int64_t heads, int64_t dim, int64_t capacity,
                                 int64_t length, int32_t elem_bytes, const int64_t* chosen,
@@ -213,7 +228,8 @@ int speckv_commit_round_prepare(void* const* key_pools, void* const* value_pools
                                 uint8_t* pad_rows, int64_t pad_rows_stride, int64_t pad_rows_count,
                                 const int64_t* owners, uint8_t* pad_live, int64_t pad_live_stride,
                                 const uint8_t* newly_padded, int64_t np_stride_b, int64_t* positions,
-                                int64_t positions_stride_b, int64_t* past_positions, void** plan);
+                                int64_t positions_stride_b, int64_t* past_positions,
+                                const int64_t* row_table, int64_t pool_rows, void** plan);
 int speckv_plan_launch(const void* plan, void* stream);
 void speckv_plan_release(void* plan);
 
@@ -399,7 +415,7 @@ int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
                                const uint32_t* bits, int64_t row_words, const int32_t* first_col,
                                void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
                                int64_t rows, int64_t kv_len, int64_t dim, float scale,
-                               int32_t dtype, void* stream);
+                               int32_t dtype, const int64_t* row_table, int64_t kv_batch, void* stream);
 
 #ifdef __cplusplus
 }

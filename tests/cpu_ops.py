@@ -18,7 +18,8 @@ def _np(t):
     return t.numpy()
 
 
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True):
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None):
+    assert row_table is None, 'the CPU stand-ins cover caches without a row table'
     def go():
         for kp, vp, ks, vs in zip(key_pools, value_pools, key_srcs, value_srcs):
             oracle.append(_np(kp), _np(vp), _np(ks), _np(vs), length)
@@ -28,7 +29,8 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=Tru
     return go
 
 
-def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width):
+def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width, row_table=None):
+    assert row_table is None, 'the CPU stand-ins cover caches without a row table'
     for kp, vp in zip(key_pools, value_pools):
         bad = oracle.compact_suffix(_np(kp), _np(vp), batch, length, chosen.numpy(), past, extension)
         assert bad == 0

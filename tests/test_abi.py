@@ -50,9 +50,16 @@ def test_argument_errors_are_reported_without_a_launch(lib):
     nul = (ctypes.c_void_p * 1)(None)
     strides = _lib.i64_array([0, 0, 0])
     with pytest.raises(_lib.SpecKVError, match='layers=0'):
-        _lib.call('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None)
+        _lib.call('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None, 0, None)
     with pytest.raises(_lib.SpecKVError, match='null pool'):
         _lib.call('speckv_move_rows', nul, nul, 1, None, None, 1, 1, 1, 8, 8, 4, 2, None)
+    pools = (ctypes.c_void_p * 1)(16)  # never dereferenced: the row-table check comes first
+    table = (ctypes.c_int64 * 1)(0)
+    with pytest.raises(_lib.SpecKVError, match="row table needs the pools' row count"):
+        _lib.call('speckv_append_rows', pools, pools, pools, pools, 1, 1, 1, 1, 8, 8, 0, strides, strides, 2,
+                  ctypes.cast(table, ctypes.c_void_p), 0, None)
+    with pytest.raises(_lib.SpecKVError, match='pool rows for'):
+        _lib.call('speckv_compact_suffix', pools, pools, 1, 4, 1, 8, 8, 8, None, 0, 0, 0, 0, 1, 2, None, 2, None)
     with pytest.raises(_lib.SpecKVError, match='invalid committed path width'):
         _lib.call('speckv_pad_verified_path', None, 0, 0, None, 0, 0, None, 1, 4, 9, 0, 0, None, None, None, 0, 0,
                   None, 0, None)
@@ -67,10 +74,11 @@ def test_prepared_launch_host_side(lib):
     nul = (ctypes.c_void_p * 1)(None)
     strides = _lib.i64_array([0, 0, 0])
     with pytest.raises(_lib.SpecKVError, match='layers=0'):
-        _lib.prepare('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None)
+        _lib.prepare('speckv_append_rows', nul, nul, nul, nul, 0, 1, 1, 1, 8, 8, 0, strides, strides, 2, None, 0,
+                     None)
     pools = (ctypes.c_void_p * 1)(16)  # never dereferenced: batch 0 moves nothing
     plan = _lib.prepare('speckv_append_rows', pools, pools, pools, pools, 1, 0, 1, 1, 8, 8, 0, strides, strides, 2,
-                        None)
+                        None, 0, None)
     assert plan.handle
     plan()
     plan()  # a plan can be launched again
