@@ -23,6 +23,8 @@ Reported (one JSON line on rank 0):
              this library's launches beside the reference's torch sequence
   history_step the accepted-feature gather + rollout-history append of a round,
              one launch beside the reference's gather + index_copy_ sequence
+  release_step releasing a quarter of the sequences: the reference's swap_remove
+             (history moves) against a row-table cache (table rewrite, no KV bytes)
 
 ``--impl reference`` times the CPU restatement of the reference's path (the
 reference is Python/torch and cannot run on the GPU host) on the host cores.
@@ -400,6 +402,7 @@ def run_ours(args):
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
     draft = measure_draft(st) if rank == 0 else None
     history = measure_history(st) if rank == 0 else None
+    release = measure_release(st) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
     append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
     append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
@@ -434,6 +437,7 @@ def run_ours(args):
         'e2e': e2e,
         'draft_step': draft,
         'history_step': history,
+        'release_step': release,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(wl, budget_s=12.0)
@@ -583,6 +587,51 @@ def measure_history(st, iters=20, warmup=3, hidden=2048):
             'timing': 'device time per step (steps queued behind a GPU spin); launch_bound_us: back to back on an '
                       'idle GPU, host launch cost included',
             'bit_exact_vs_torch_sequence': bool(same)}
+
+
+def measure_release(st, fraction=0.25, spin_ms=8.0):
+    """Release of `fraction` of the sequences after the timed rounds, at the workload's layers,
+    batch and length: the reference's swap_remove (the surviving tail sequences' whole
+    histories moved into the holes, all layers in one move_rows launch; device time with the
+    launch queued behind a GPU spin) against a row-table cache, where the release rewrites the
+    table (host time of the call, which stages and uploads the table). The table release moves
+    no KV bytes whatever the pools' size, so its cache holds a one-position history."""
+    import torch
+    from analysis_spec_b200.opd_static_cache import OPDStaticCache, swap_remove_plan
+    wl, dev = st.wl, st.device
+    rng = np.random.RandomState(17)
+    batch = st.cache.layers[0].batch_size
+    finished = [False] * batch
+    for i in rng.choice(batch, size=max(1, int(batch * fraction)), replace=False):
+        finished[i] = True
+    keep, sources, dests = swap_remove_plan(finished)
+    layer = st.cache.layers[0]
+    moved = len(sources) * 2 * wl.layers * layer.key_pool.shape[1] * layer.length * layer.key_pool.shape[-1] * \
+        layer.key_pool.element_size()
+    src = torch.tensor(sources, device=dev, dtype=torch.long)
+    dst = torch.tensor(dests, device=dev, dtype=torch.long)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(spin_ms * 1e-3 * 2.0e9))
+    a.record()
+    st.cache.swap_remove(len(keep), src, dst)
+    b.record()
+    torch.cuda.synchronize()
+    physical_us = a.elapsed_time(b) * 1e3
+    table_cache = OPDStaticCache(256, batch_capacity=batch, row_table=True)
+    one = torch.zeros(batch, layer.key_pool.shape[1], 1, layer.key_pool.shape[-1], device=dev, dtype=st.dtype)
+    table_cache.update_layers([one] * wl.layers, [one] * wl.layers)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    table_cache.swap_remove(len(keep), sources, dests)
+    host_us = (time.perf_counter() - t0) * 1e6
+    torch.cuda.synchronize()
+    return {'released': len(finished) - len(keep), 'moved_by_swap_remove': len(sources),
+            'swap_remove_us_device': round(physical_us, 2), 'swap_remove_bytes': moved,
+            'swap_remove_gbs': round(moved / (physical_us * 1e-6) / 1e9, 1) if physical_us > 0 else None,
+            'row_table_us_host': round(host_us, 2), 'row_table_kv_bytes': 0,
+            'shape': f'{wl.layers} layers, batch {batch}, length {layer.length}, {layer.key_pool.shape[1]} kv heads '
+                     f'x {layer.key_pool.shape[-1]}'}
 
 
 def measure_e2e(st, args, world):
