@@ -103,3 +103,51 @@ def test_tree_verify_forward_matches_sdpa_and_greedy_acceptance():
     agree = (results['bits'].argmax(-1) == ref.argmax(-1)).float().mean().item()
     assert agree >= 0.95, agree
     assert lengths['dense'] == lengths['sdpa'] and lengths['bits'] == lengths['sdpa'], lengths
+
+
+def test_tree_verify_forward_through_a_row_table():
+    """A row-table cache on the real model: 2B prompts prefilled, the B decoys among them
+    released through the table (no history moved, the survivors scattered over the pool
+    rows), then the tree verify forward of the survivors with the registered attention
+    matches transformers' SDPA on a table-free cache holding only those prompts."""
+    from analysis_spec_b200.opd_static_cache import swap_remove_plan
+    name = register()
+    model = _model()
+    ids, mask2d, parents, tokens, positions = _inputs()
+    rng = np.random.RandomState(9)
+    real_at = [1, 2, 5, 6]  # where the B real prompts sit among 2B
+    all_ids = rng.randint(0, VOCAB, size=(2 * B, PROMPT))
+    all_mask = np.ones((2 * B, PROMPT), dtype=np.int64)
+    for j, i in enumerate(real_at):
+        all_ids[i], all_mask[i] = ids[j], mask2d[j]
+    cache = OPDStaticCache(64, batch_capacity=2 * B, row_table=True)
+    am = torch.from_numpy(all_mask).cuda()
+    pos = (am.cumsum(-1) - 1).clamp(min=0)
+    with torch.no_grad():  # the table is still the identity: transformers' SDPA reads the views as they are
+        model(input_ids=torch.from_numpy(all_ids).cuda(), attention_mask=am, position_ids=pos,
+              past_key_values=cache, use_cache=True)
+    keep, sources, dests = swap_remove_plan([i not in real_at for i in range(2 * B)])
+    cache.swap_remove(len(keep), sources, dests)
+    assert cache.row_table == keep and keep != sorted(keep)
+    perm = [real_at.index(k) for k in keep]  # logical sequence -> prompt
+    pad_np = np.zeros((B, PROMPT + ROWS), dtype=bool)
+    pad_np[:, :PROMPT] = mask2d[perm] == 0
+    tree = PackedTree(torch.from_numpy(parents[perm]).cuda(), torch.from_numpy(tokens[perm]).cuda(),
+                      torch.zeros(B, ROWS, dtype=torch.long, device='cuda'), DEPTH)
+    mask = tree.attention_mask(PROMPT, torch.bfloat16, torch.from_numpy(pad_np).cuda())
+    logits = _verify(model, cache, tree, tokens[perm], positions[perm], mask, name)
+    assert cache.get_seq_length() == PROMPT + ROWS
+    ref_cache = _prefill(model, ids, mask2d)
+    ref_pad = np.zeros((B, PROMPT + ROWS), dtype=bool)
+    ref_pad[:, :PROMPT] = mask2d == 0
+    ref_tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(tokens).cuda(),
+                          torch.zeros(B, ROWS, dtype=torch.long, device='cuda'), DEPTH)
+    ref_mask = ref_tree.attention_mask(PROMPT, torch.bfloat16, torch.from_numpy(ref_pad).cuda())
+    ref = _verify(model, ref_cache, ref_tree, tokens, positions, ref_mask, 'sdpa')[perm]
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+    scale = ref.abs().max().item()
+    err = (logits - ref).abs()
+    assert err.max().item() <= 2e-2 * max(scale, 1.0), (err.max().item(), scale)
+    assert err.mean().item() <= 2e-3 * max(scale, 1.0), (err.mean().item(), scale)
+    assert (logits.argmax(-1) == ref.argmax(-1)).float().mean().item() >= 0.95
