@@ -82,8 +82,13 @@ struct Sm100Args {
   int batch, q_heads, kv_heads, group, rows, kv_len, mtiles;
   float scale_log2;       // softmax scale * log2(e)
   unsigned long long* err;
-  const int64_t* row_table;  // pair kernel: K/V pool row of each sequence (NULL: row b)
-  int kv_batch;              // K/V rows
+};
+
+// K/V rows of each sequence for the pair kernel (NULL map: sequence b is row b); a separate
+// kernel argument so the table-free kernels' argument block stays as it was.
+struct KvRows {
+  const int64_t* map;
+  int rows;
 };
 
 // ---------------------------------------------------------------------------
@@ -766,10 +771,12 @@ struct Item {
 // tiles i with i % 2 == w); S_w of tile i and the P.V of tile i - 1 are issued in turn,
 // so the K and V rings are consumed in order. Warpgroup 1 hands its running max and sum
 // to warpgroup 0 through shared memory (C_XCHG, a bounded wait), which merges O0 and O1.
-template <typename T, bool SPLIT>
+// TABLE: the K/V rows of sequence b come from a.row_table[b] (a separate instantiation, so
+// the table-free kernel carries no trace of it).
+template <typename T, bool SPLIT, bool TABLE>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                     const Sm100Args a) {
+                     const Sm100Args a, const KvRows kvr) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -855,9 +862,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       for (int k = 0; ok && item_at(k, it); ++k) {
         const int t0 = first_tile(it.b);
         int kb = it.b;  // K/V row of the sequence: through the row table when there is one
-        if (a.row_table != nullptr) {
-          const long long p = a.row_table[it.b];
-          if (p < 0 || p >= a.kv_batch) {
+        if (TABLE) {
+          const long long p = kvr.map[it.b];
+          if (p < 0 || p >= kvr.rows) {
             record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
             kb = 0;
           } else {
@@ -1266,9 +1273,10 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-template <typename T, bool SPLIT>
-int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, cudaStream_t stream) {
-  auto kern = attn_pair_kernel<T, SPLIT>;
+template <typename T, bool SPLIT, bool TABLE>
+int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, const KvRows& kvr,
+                cudaStream_t stream) {
+  auto kern = attn_pair_kernel<T, SPLIT, TABLE>;
   // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
   // per thread; any other count could leave the increase waiting for registers.
   static int regs = -1;
@@ -1283,7 +1291,7 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s
   const long long pairs = ((long long)s.group * s.rows + 2 * BM - 1) / (2 * BM);
   const long long items = (long long)s.batch * s.kv_heads * pairs;
   const long long grid = items < sm_count() ? items : sm_count();
-  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, s);
+  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, s, kvr);
   return check_launch("speckv_tree_attention_bits(sm100)");
 }
 
@@ -1330,14 +1338,21 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   s.mtiles = (int)((s.group * a.rows + BM - 1) / BM);
   s.scale_log2 = a.scale * 1.4426950408889634f;
   s.err = err;
-  s.row_table = a.row_table;
-  s.kv_batch = (int)a.kv_batch;
+  const KvRows kvr{a.row_table, (int)a.kv_batch};
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
     // at most one 128-row tile per (sequence, KV head): the two warpgroups split the keys
-    if ((long long)s.group * s.rows <= BM)
-      return bf ? launch_pair<__nv_bfloat16, true>(mk, mv, s, stream) : launch_pair<__half, true>(mk, mv, s, stream);
-    return bf ? launch_pair<__nv_bfloat16, false>(mk, mv, s, stream) : launch_pair<__half, false>(mk, mv, s, stream);
+    const bool split = (long long)s.group * s.rows <= BM, table = kvr.map != nullptr;
+    if (bf) {
+      if (split) return table ? launch_pair<__nv_bfloat16, true, true>(mk, mv, s, kvr, stream)
+                              : launch_pair<__nv_bfloat16, true, false>(mk, mv, s, kvr, stream);
+      return table ? launch_pair<__nv_bfloat16, false, true>(mk, mv, s, kvr, stream)
+                   : launch_pair<__nv_bfloat16, false, false>(mk, mv, s, kvr, stream);
+    }
+    if (split) return table ? launch_pair<__half, true, true>(mk, mv, s, kvr, stream)
+                            : launch_pair<__half, true, false>(mk, mv, s, kvr, stream);
+    return table ? launch_pair<__half, false, true>(mk, mv, s, kvr, stream)
+                 : launch_pair<__half, false, false>(mk, mv, s, kvr, stream);
   }
   const int min_group = a.mask_dtype == SPECKV_F32 ? mask_min_group<float>() : mask_min_group<uint16_t>();
   if (a.mask != nullptr && s.group >= min_group) {
