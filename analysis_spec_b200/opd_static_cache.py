@@ -376,6 +376,7 @@ class OPDStaticCache(Cache):
         if max_retained_tokens and any(layer.capacity > max_retained_tokens for layer in self.layers):
             self.layers.clear()
             self._scratch.clear()
+            self._rows, self._rows_dev = [], None  # the next pools start with a fresh table
 
     def scratch(self, pool, shape):
         """Reusable (rows, heads, chunk, dim) tile buffer keyed by device/dtype/geometry."""

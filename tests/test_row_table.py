@@ -167,3 +167,24 @@ def test_row_table_attention_and_device_commit_match_logical_order():
     _ops.commit_round([kpool], [vpool], batch, past + rows, chosen, past, packet, row_table=bad)
     torch.cuda.synchronize()
     assert _ops.device_error() == ('row table', pool_rows + 3)
+
+
+@pytest.mark.gpu
+def test_row_table_survives_pool_release_and_larger_rollout():
+    """end_rollout that drops the pools also drops the table; a later, larger rollout starts
+    from a fresh identity table."""
+    from analysis_spec_b200 import _ops
+    from analysis_spec_b200.opd_static_cache import OPDStaticCache
+    cache = OPDStaticCache(256, batch_capacity=4, row_table=True)
+    k = torch.randn(4, 2, 8, 128, device='cuda').to(torch.bfloat16)
+    cache.update(k, k, 0)
+    cache.swap_remove(2, [3], [0])
+    assert cache.row_table == [3, 1]
+    cache.end_rollout(max_retained_tokens=1)
+    big = torch.randn(9, 2, 8, 128, device='cuda').to(torch.bfloat16)
+    cache.begin_rollout(9, 9)
+    keys, _ = cache.update(big, big, 0)
+    assert cache.row_table == list(range(9))
+    assert torch.equal(keys[torch.tensor(cache.row_table, device='cuda')], big)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
