@@ -1240,9 +1240,29 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Encoded maps of the views seen last on this thread: the verify loop hands every layer's
+// K/V cache views again each round, so their maps are encoded once.
+struct KvMapEntry {
+  const void* base;
+  long long st[3], batch, heads, len;
+  int dtype;
+  CUtensorMap map;
+};
+constexpr int kKvMapCache = 256;
+
 // 4-D map over a (batch, heads, len, 128) strided view: dims (d, len, heads, batch).
 bool make_kv_map(CUtensorMap* map, const void* base, const long long* st, long long batch, long long heads,
                  long long len, int dtype) {
+  thread_local KvMapEntry cache[kKvMapCache];
+  thread_local int used = 0, next = 0;
+  for (int i = 0; i < used; ++i) {
+    const KvMapEntry& e = cache[i];
+    if (e.base == base && e.st[0] == st[0] && e.st[1] == st[1] && e.st[2] == st[2] && e.batch == batch &&
+        e.heads == heads && e.len == len && e.dtype == dtype) {
+      *map = e.map;
+      return true;
+    }
+  }
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)batch};
@@ -1253,7 +1273,20 @@ bool make_kv_map(CUtensorMap* map, const void* base, const long long* st, long l
                     4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return res == CUDA_SUCCESS;
+  if (res != CUDA_SUCCESS) return false;
+  KvMapEntry& e = cache[next];
+  e.base = base;
+  e.st[0] = st[0];
+  e.st[1] = st[1];
+  e.st[2] = st[2];
+  e.batch = batch;
+  e.heads = heads;
+  e.len = len;
+  e.dtype = dtype;
+  e.map = *map;
+  next = (next + 1) % kKvMapCache;
+  if (used < kKvMapCache) ++used;
+  return true;
 }
 
 template <typename T, int MODE, typename MT>
@@ -1266,11 +1299,21 @@ int launch_sm100(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& 
   return check_launch("speckv_tree_attention(sm100)");
 }
 
+constexpr int kMaxAttnDevices = 64;
+
+int current_device() {
+  int dev = 0;
+  return cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxAttnDevices ? dev : -1;
+}
+
 int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return 148;
-  return n > 0 ? n : 148;
+  static int cached[kMaxAttnDevices] = {0};
+  const int dev = current_device();
+  if (dev >= 0 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  cached[dev] = n;
+  return n;
 }
 
 template <typename T, bool SPLIT, bool TABLE>
@@ -1287,7 +1330,12 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s
   if (regs != kRegsLaunch)
     return fail(SPECKV_ENOSUPPORT, "speckv_tree_attention_bits: kernel compiled with %d registers per thread, "
                 "the register split needs %d", regs, kRegsLaunch);
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+  static bool smem_set[kMaxAttnDevices] = {false};  // the attribute is per device: set it once on each
+  const int dev = current_device();
+  if (dev < 0 || !smem_set[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+    if (dev >= 0) smem_set[dev] = true;
+  }
   const long long pairs = ((long long)s.group * s.rows + 2 * BM - 1) / (2 * BM);
   const long long items = (long long)s.batch * s.kv_heads * pairs;
   const long long grid = items < sm_count() ? items : sm_count();
