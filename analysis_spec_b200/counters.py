@@ -77,6 +77,13 @@ class AcceptanceCounters:
         self._work = dist.all_reduce(vec, group=self.group, async_op=True)
         self._vec = vec
 
+    def fence(self, stream=None):
+        """Orders `stream` (default: the current one) after the reductions queued so far. Call it
+        before a kernel that keeps every SM busy (the persistent attention): an all_reduce kernel
+        still waiting for a peer rank would otherwise hold SMs that kernel's CTAs wait for."""
+        if self._cuda and self.distributed:
+            (stream or torch.cuda.current_stream(self.device)).wait_stream(self._stream)
+
     def finish(self):
         """Waits for the outstanding reductions and returns the totals as a dict."""
         if self._cuda:
