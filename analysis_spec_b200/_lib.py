@@ -56,6 +56,8 @@ SIGNATURES = {
     'speckv_history_pack': [_p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p],
     'speckv_expansion_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p],
     'speckv_version': [],
+    'speckv_attention_launches': [_pi64, _pi64],
+    'speckv_attention_test_hooks': [_i64, _i32],
 }
 
 # entries with a prepare / launch split (speckv_<name>_prepare + speckv_plan_launch)
@@ -136,13 +138,22 @@ def call(name, *args):
 
 
 class Plan:
-    """A prepared launch of entry point `name` (see speckv_plan_launch); freed with the object."""
+    """A prepared launch of entry point `name` (see speckv_plan_launch); freed with the object.
+    It launches with the GPU it was prepared on current (the C side refuses any other)."""
 
-    def __init__(self, name, handle, stream):
-        self.name, self.handle, self.stream = name, handle, stream
+    def __init__(self, name, handle, stream, device):
+        self.name, self.handle, self.stream, self.device = name, handle, stream, device
 
     def __call__(self):
         """Enqueues the prepared kernel (profiled under the entry point's own name)."""
+        if self.device >= 0:
+            import torch
+            if torch.cuda.current_device() != self.device:
+                with torch.cuda.device(self.device):
+                    return self._launch()
+        return self._launch()
+
+    def _launch(self):
         lib = load()
         if profile.enabled:
             import torch
@@ -171,7 +182,8 @@ def prepare(name, *args):
     status = getattr(lib, name + '_prepare')(*args[:-1], ctypes.byref(handle))
     if status != SPECKV_OK:
         raise SpecKVError(name + '_prepare', status, lib.speckv_last_error().decode(errors='replace'))
-    return Plan(name, handle, args[-1])
+    import torch
+    return Plan(name, handle, args[-1], torch.cuda.current_device() if torch.cuda.is_available() else -1)
 
 
 def ptr_array(values):

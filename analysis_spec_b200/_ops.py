@@ -2,11 +2,40 @@
 libspeckv call on the current CUDA stream of the tensors' device.
 
 Every function here requires CUDA tensors and raises otherwise; there is no
-CPU path in the product.
+CPU path in the product. The library launches on the current GPU, so every
+entry point here first makes the GPU of its first CUDA tensor argument current
+(for the duration of the call); the C side refuses operands of another GPU.
 """
+import functools
+
 import torch
 
 from . import _lib
+
+
+def _first_device(values):
+    """Index of the GPU holding the first CUDA tensor among `values` (tensors or lists of them)."""
+    for v in values:
+        if isinstance(v, torch.Tensor):
+            if v.is_cuda:
+                return v.device.index
+        elif isinstance(v, (list, tuple)) and v and isinstance(v[0], torch.Tensor) and v[0].is_cuda:
+            return v[0].device.index
+    return None
+
+
+def _on_device(fn):
+    """Runs `fn` with the GPU of its first CUDA tensor argument current."""
+    @functools.wraps(fn)
+    def wrapper(*args, **kwargs):
+        dev = _first_device(args)
+        if dev is None:
+            dev = _first_device(kwargs.values())
+        if dev is None or dev == torch.cuda.current_device():
+            return fn(*args, **kwargs)
+        with torch.cuda.device(dev):
+            return fn(*args, **kwargs)
+    return wrapper
 
 _DTYPE_CODE = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16, torch.float16: _lib.F16}
 
@@ -49,6 +78,7 @@ def _row_table(fn, row_table, batch, pool_rows):
     return row_table.data_ptr(), pool_rows
 
 
+@_on_device
 def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None):
     """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers);
     with `row_table` sequence b goes to pool row row_table[b].
@@ -100,6 +130,7 @@ def _issue(name, calls, launch):
     return go
 
 
+@_on_device
 def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extension, width, row_table=None):
     """Accepted-suffix compaction of every layer (one launch per 64 layers); with `row_table`
     sequence b is pool row row_table[b]."""
@@ -118,6 +149,7 @@ def compact_suffix(key_pools, value_pools, batch, length, chosen, past, extensio
                   es, table, table_rows, _stream(chosen))
 
 
+@_on_device
 def commit_round(key_pools, value_pools, batch, length, chosen, past, packet, newly_padded=None, positions=None,
                  past_positions=None, pad_rows=None, owners=None, pad_live=None, launch=True, row_table=None):
     """Compaction of every layer + position/padding update of one verify round in one launch,
@@ -182,6 +214,7 @@ def remap_scratch_elements(new_batch, heads, dim, length, element_size):
     return (nbytes + element_size - 1) // element_size
 
 
+@_on_device
 def remap_rows(key_pools, value_pools, indices, length, scratch=None):
     """pool[:n] = pool[indices] over [0, length) for every layer."""
     _require_cuda(key_pools[0], indices)
@@ -197,6 +230,7 @@ def remap_rows(key_pools, value_pools, indices, length, scratch=None):
                   _stream(indices))
 
 
+@_on_device
 def remap_rows_static(key_pools, value_pools, indices, length):
     """remap_rows without scratch from the caller: uses the library's fixed device array
     (for callers that cannot allocate; concurrent calls on one device must be serialised)."""
@@ -211,6 +245,7 @@ def remap_rows_static(key_pools, value_pools, indices, length):
                   indices.numel(), bcap, heads, dim, capacity, length, es, _stream(indices))
 
 
+@_on_device
 def move_rows(key_pools, value_pools, sources, destinations, length):
     """pool[destinations[j]] = pool[sources[j]] over [0, length) for every layer."""
     _require_cuda(key_pools[0], sources, destinations)
@@ -233,6 +268,7 @@ def _contig_long(name, t):
     return t if t.is_contiguous() else t.contiguous()
 
 
+@_on_device
 def pack_tree(full_parents, full_contexts, all_tokens, chosen, out_parents, out_tokens, out_contexts):
     _require_cuda(full_parents, full_contexts, all_tokens, chosen, out_parents, out_tokens, out_contexts)
     batch, full_count = full_parents.shape
@@ -250,6 +286,7 @@ def pack_tree(full_parents, full_contexts, all_tokens, chosen, out_parents, out_
               out_contexts.data_ptr(), out_parents.stride(0), _stream(chosen))
 
 
+@_on_device
 def trace_path(parents, tokens, contexts, samples, eos, out_tokens, out_indices, out_contexts, lengths):
     _require_cuda(parents, tokens, contexts, samples, out_tokens, out_indices, out_contexts, lengths)
     batch, rows = samples.shape
@@ -273,6 +310,7 @@ def _check_pad_outputs(tokens, indices, mask):
         raise ValueError('padded outputs must be int64, int64, bool')
 
 
+@_on_device
 def pad_verified_path(path_tokens, path_indices, lengths, width, past, eos, tokens, indices, mask, last):
     _require_cuda(path_tokens, path_indices, lengths, tokens, indices, mask, last)
     _check_pad_outputs(tokens, indices, mask)
@@ -284,6 +322,7 @@ def pad_verified_path(path_tokens, path_indices, lengths, width, past, eos, toke
               tokens.stride(0), tokens.stride(1), last.data_ptr(), last.stride(0), _stream(path_tokens))
 
 
+@_on_device
 def pad_schedule(path_tokens, path_indices, lengths, past, eos, tokens, indices, mask, last, packet,
                  snapshot=None):
     _require_cuda(path_tokens, path_indices, lengths, tokens, indices, mask, last, packet, snapshot)
@@ -305,6 +344,7 @@ def pad_schedule(path_tokens, path_indices, lengths, past, eos, tokens, indices,
               packet.stride(0), packet.stride(1), _ptr(snapshot), _stream(path_tokens))
 
 
+@_on_device
 def tree_mask(parents, past, steps, mask, pad=None):
     """Dense additive ancestor mask (batch, 1, rows, past + rows); `pad` (batch, >= cols) bool forces columns off."""
     _require_cuda(parents, mask, pad)
@@ -324,6 +364,7 @@ def tree_mask(parents, past, steps, mask, pad=None):
     torch.autograd.graph.increment_version(mask)
 
 
+@_on_device
 def position_update(newly_padded, past, positions, past_positions, pad_rows=None, owners=None, pad_live=None):
     _require_cuda(newly_padded, positions, past_positions, pad_rows, owners, pad_live)
     batch, width = newly_padded.shape
@@ -340,6 +381,7 @@ def position_update(newly_padded, past, positions, past_positions, pad_rows=None
               _stream(newly_padded))
 
 
+@_on_device
 def tree_attention(query, key, value, mask, scale, out=None):
     """GQA attention (batch, Hq, R, D) x (batch, Hkv, L, D) -> (batch, R, Hq, D) with an additive mask."""
     _require_cuda(query, key, value, mask)
@@ -375,6 +417,7 @@ def visibility_words(cols):
     return 4 * (-(-cols // 128))
 
 
+@_on_device
 def tree_mask_bits(parents, past, steps, bits, first_col, pad=None):
     """Bit-packed tree visibility (batch, rows, words) int32 + first visible column per sequence."""
     _require_cuda(parents, bits, first_col, pad)
@@ -403,6 +446,7 @@ def _check_qkv(query, key, value, any_kv_rows=False):
         raise ValueError('key/value shapes do not match the query')
 
 
+@_on_device
 def tree_attention_bits(query, key, value, bits, first_col, scale, out=None, row_table=None):
     """GQA attention with visibility from tree_mask_bits (no dense mask read). With `row_table`
     the K/V of sequence b are key[row_table[b]] / value[row_table[b]] (key / value then hold
@@ -463,6 +507,7 @@ def _bits_operands(fn, mask, bits, first_col):
     return bits.shape[2]
 
 
+@_on_device
 def causal_mask(mask, past, pad=None, bits=None, first_col=None):
     """mask[b, 0, r, c] = 0 if c <= past + r and not pad[b, c] else finfo(dtype).min (one launch);
     with `bits` / `first_col` the same visibility bit-packed for tree_attention_bits."""
@@ -475,6 +520,7 @@ def causal_mask(mask, past, pad=None, bits=None, first_col=None):
     torch.autograd.graph.increment_version(mask)
 
 
+@_on_device
 def expansion_mask(mask, init_length, seen, pad=None, bits=None, first_col=None):
     """mask[b, 0, r, c] = 0 if (c < init_length or c == seen[b, r, 0]) and not pad[b, c], else
     finfo(dtype).min; `seen` (batch, query[, 1]) int64 (one launch)."""
@@ -511,6 +557,7 @@ def _history_layout_key(fields, n, pool_rows):
     return tuple(key)
 
 
+@_on_device
 def history_append(fields, owners, pool_rows, n, src_rows=None, cache=None):
     """One launch over up to four history fields. Each field is a tuple
     (pool, src, index, gathered, start, width): pool (pool_rows, capacity, *elem) or None;
@@ -583,6 +630,7 @@ def history_append(fields, owners, pool_rows, n, src_rows=None, cache=None):
               _stream(fields[0][1]))
 
 
+@_on_device
 def history_pack(dst, pool, offsets, rows, max_length):
     """dst (total, *elem) contiguous <- the used prefix of each pool row; offsets int64 (rows + 1,)."""
     _require_cuda(dst, pool, offsets)
@@ -595,6 +643,7 @@ def history_pack(dst, pool, offsets, rows, max_length):
               int(max_length), _stream(pool))
 
 
+@_on_device
 def mask_bits(mask, bits, first_col, nonbinary):
     """Visibility bits of a dense additive (batch, 1, rows, columns) mask (any strides): bit set
     iff the entry is 0; lowest-value / -inf entries masked; any other value sets nonbinary[0]."""

@@ -1,12 +1,20 @@
 // C-ABI entries of the tree-verify attention: validate arguments and pick the
-// kernel for the shape (tcgen05 kernel for head dim 128 in bf16/fp16 with
-// 16-byte aligned rows, the CUDA-core kernel otherwise).
+// kernel for the shape. Head dim 128 in bf16 / fp16 (every verify and draft
+// attention of the Qwen2.5 geometries) runs only on the tcgen05 kernels; a view
+// of that shape they cannot read (a base or stride that is not 16-byte aligned)
+// is refused with SPECKV_ENOSUPPORT instead of silently taking a slower path.
+// The CUDA-core kernel serves the other head dims and fp32. Both paths count
+// their launches (speckv_attention_launches).
 #include "common.cuh"
 #include "attention.cuh"
+
+#include <atomic>
 
 using namespace speckv;
 
 namespace {
+
+std::atomic<long long> g_tensor_core_launches{0}, g_cuda_core_launches{0};
 
 int check(const char* fn, const void* q, const int64_t* qs, const void* k, const int64_t* ks, const void* v,
           const int64_t* vs, const void* out, int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t rows,
@@ -51,9 +59,23 @@ void fill(AttnArgs& a, const void* q, const int64_t* qs, const void* k, const in
   a.kv_batch = batch;
 }
 
-int launch(const AttnArgs& a, cudaStream_t s) {
-  if (sm100_supported(a)) return attention_sm100(a, s);
-  return attention_generic(a, s);
+int launch(const char* fn, const AttnArgs& a, cudaStream_t s) {
+  int st = check_current_device(fn, {a.q, a.k, a.out, a.mask != nullptr ? a.mask : a.bits});
+  if (st) return st;
+  const bool tensor_shape = a.dim == 128 && (a.dtype == SPECKV_BF16 || a.dtype == SPECKV_F16);
+  if (tensor_shape) {
+    if (!sm100_supported(a))
+      return fail(SPECKV_ENOSUPPORT,
+                  "%s: head dim 128 in bf16 / fp16 runs on the tensor-core kernel only, which needs 16-byte aligned "
+                  "Q / K / V / output bases and strides (and visibility rows of a multiple of 4 words), batch <= "
+                  "2^20 and kv_len <= 2^30; this view does not qualify", fn);
+    st = attention_sm100(a, s);
+    if (st == SPECKV_OK) ++g_tensor_core_launches;
+    return st;
+  }
+  st = attention_generic(a, s);
+  if (st == SPECKV_OK) ++g_cuda_core_launches;
+  return st;
 }
 
 }  // namespace
@@ -74,7 +96,7 @@ extern "C" int speckv_tree_attention(const void* q, const int64_t* q_strides,
   fill(a, q, q_strides, k, k_strides, v, v_strides, out, batch, q_heads, kv_heads, rows, kv_len, dim, scale, dtype);
   a.mask = mask;
   a.mask_dtype = mask_dtype;
-  return launch(a, static_cast<cudaStream_t>(stream));
+  return launch(fn, a, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
@@ -105,5 +127,19 @@ extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_stride
       return fail(SPECKV_ENOSUPPORT, "%s: row tables need the tensor-core path (head dim 128, bf16 / fp16, "
                   "16-byte aligned rows)", fn);
   }
-  return launch(a, static_cast<cudaStream_t>(stream));
+  return launch(fn, a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int speckv_attention_launches(int64_t* tensor_core, int64_t* cuda_core) {
+  if (tensor_core == nullptr || cuda_core == nullptr)
+    return fail(SPECKV_EINVAL, "speckv_attention_launches: null output");
+  *tensor_core = g_tensor_core_launches.load();
+  *cuda_core = g_cuda_core_launches.load();
+  return SPECKV_OK;
+}
+
+extern "C" int speckv_attention_test_hooks(int64_t wait_limit_ns, int32_t withhold_q_arrival) {
+  if (wait_limit_ns < 0 || withhold_q_arrival < 0 || withhold_q_arrival > 1)
+    return fail(SPECKV_EINVAL, "speckv_attention_test_hooks: wait limit >= 0 and a 0 / 1 switch expected");
+  return attention_test_hooks(wait_limit_ns, withhold_q_arrival);
 }

@@ -30,4 +30,9 @@ int attention_generic(const AttnArgs& a, cudaStream_t s);
 bool sm100_supported(const AttnArgs& a);
 int attention_sm100(const AttnArgs& a, cudaStream_t s);
 
+// Test hooks of the tensor-core kernels on the current device (synchronous copies):
+// the bounded waits' limit in ns (<= 0: the default 2 s) and whether CTA 0 of the
+// visibility-bits kernel withholds its first Q-tile arrival.
+int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival);
+
 }  // namespace speckv

@@ -66,6 +66,19 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t S_COL0 = 0, O_COL = 256;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
+// Test hooks (speckv_attention_test_hooks): a shorter limit for the bounded waits
+// (0 = kWaitNs) and a switch that makes CTA 0's first softmax warpgroup withhold its
+// first Q-tile arrival, so that the MMA warp's wait runs out with no copy or MMA in
+// flight. Both stay 0 in normal use; they are read only on the slow path of a wait
+// and once per CTA.
+__device__ unsigned long long g_wait_limit_ns = 0ull;
+__device__ int g_withhold_q_arrival = 0;
+
+__device__ __forceinline__ unsigned long long wait_limit() {
+  const unsigned long long v = *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+  return v != 0ull ? v : kWaitNs;
+}
+
 // barrier slots (8 bytes each) after BAR_OFF
 enum { B_KV_FULL = 0, B_KV_EMPTY = 2, B_S_FULL = 4, B_S_FREE = 6, B_P_FULL = 8, B_O_DONE = 9, B_Q_READY = 10,
        B_DRAIN = 11, B_ABORT = 12, TMEM_SLOT = 13, B_M_FULL = 14, B_M_EMPTY = 16 };
@@ -142,12 +155,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           unsigned long long* err, int where) {
   if (mbar_try(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
+  const unsigned long long t0 = global_ns(), limit = wait_limit();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > limit) {
         *abort_flag = 1;
         record_error(err, SPECKV_DERR_TIMEOUT, where);
         return false;
@@ -157,7 +170,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 }
 
 // Time-bounded wait that ignores the abort flag: used to let in-flight asynchronous
-// work finish before the CTA releases shared memory / TMEM.
+// work finish before the CTA releases shared memory / TMEM. It keeps the full limit
+// (never the test hook's shorter one): copies in flight must land.
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = global_ns();
   while (!mbar_try(bar, parity)) {
@@ -372,10 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(vdst, &tmv, bar(B_KV_FULL + s), 0, col, kvh, b);
         tma_load_4d(vdst + kTileHalf, &tmv, bar(B_KV_FULL + s), 64, col, kvh, b);
       }
-      // After an abort, copies still in flight must land before shared memory is released.
-      if (*abort_flag) {
-        for (int it = issued - 2 < 0 ? 0 : issued - 2; it < issued; ++it) drain_wait(bar(B_KV_FULL + (it & 1)), (it >> 1) & 1);
-      }
+      // Copies still in flight must land before shared memory is released: after an abort
+      // nobody consumes them (in a normal run these phases completed long ago).
+      for (int it = issued - 2 < 0 ? 0 : issued - 2; it < issued; ++it) drain_wait(bar(B_KV_FULL + (it & 1)), (it >> 1) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -887,10 +900,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
           issued_v = cnt + 1;
         }
       }
-      if (*abort_flag) {  // loads still in flight must land before shared memory is released
-        for (int q = issued_k - 2 < 0 ? 0 : issued_k - 2; q < issued_k; ++q) drain_wait(bar(C_K_FULL + (q & 1)), (q >> 1) & 1);
-        for (int q = issued_v - 2 < 0 ? 0 : issued_v - 2; q < issued_v; ++q) drain_wait(bar(C_V_FULL + (q & 1)), (q >> 1) & 1);
-      }
+      // Loads still in flight must land before shared memory is released: after an abort
+      // (which may come after this loop ended) nobody consumes them; in a normal run
+      // these phases completed long ago and the waits return at once.
+      for (int q = issued_k - 2 < 0 ? 0 : issued_k - 2; q < issued_k; ++q) drain_wait(bar(C_K_FULL + (q & 1)), (q >> 1) & 1);
+      for (int q = issued_v - 2 < 0 ? 0 : issued_v - 2; q < issued_v; ++q) drain_wait(bar(C_V_FULL + (q & 1)), (q >> 1) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (whole warp, lane 0 issues) ----------------
@@ -1042,7 +1056,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       return m;
     };
     // Q rows of item x -> swizzled shared tile t (zeros for padding rows), then Q_FULL
-    auto write_q = [&](const Item& x) {
+    // (withheld when the test hook asks it of this CTA's first item)
+    auto write_q = [&](const Item& x, bool withhold) {
       const RowMap m = row_map(x);
       const T* qrow = static_cast<const T*>(a.q) + (long long)x.b * a.qs0 + (long long)m.hq * a.qs1 +
                       (long long)m.r * a.qs2;
@@ -1054,7 +1069,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v[cc];
       fence_proxy_async();
-      mbar_arrive(bar(C_Q_FULL + (SPLIT ? 0 : t)));
+      if (!withhold) mbar_arrive(bar(C_Q_FULL + (SPLIT ? 0 : t)));
     };
     auto next_item = [&](int& kk, Item& nx) -> bool {
       for (;; ++kk) {
@@ -1066,7 +1081,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
     bool ok = true;
     Item it;
     bool have = next_item(k, it);
-    if (have && (!SPLIT || t == 0)) write_q(it);
+    if (have && (!SPLIT || t == 0))
+      write_q(it, blockIdx.x == 0 && t == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0);
     const int i_first = SPLIT ? t : 0, i_step = SPLIT ? 2 : 1;  // this warpgroup's key tiles
     while (have) {
       const int t0 = first_tile(it.b);
@@ -1151,7 +1167,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       int kn = k + 1;
       const bool have_next = next_item(kn, nx);
       // (SPLIT: warpgroup 1's last S may still read Q tile 0; the next Q waits for the merge)
-      if (have_next && !SPLIT) write_q(nx);
+      if (have_next && !SPLIT) write_q(nx, false);
       ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
@@ -1211,7 +1227,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
       }
       tc_fence_before();
-      if (SPLIT && have_next) write_q(nx);  // O0 and O1 are read: the next item may start
+      if (SPLIT && have_next) write_q(nx, false);  // O0 and O1 are read: the next item may start
       it = nx;
       k = kn;
       have = have_next;
@@ -1344,6 +1360,14 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s
 }
 
 }  // namespace
+
+int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival) {
+  const unsigned long long lim = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : 0ull;
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_withhold_q_arrival, &withhold_q_arrival, sizeof(int));
+  if (e != cudaSuccess) return fail(SPECKV_ECUDA, "speckv_attention_test_hooks: %s", cudaGetErrorString(e));
+  return SPECKV_OK;
+}
 
 bool sm100_supported(const AttnArgs& a) {
   if (a.dim != HD || (a.dtype != SPECKV_BF16 && a.dtype != SPECKV_F16)) return false;

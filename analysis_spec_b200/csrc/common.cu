@@ -52,6 +52,26 @@ unsigned long long* device_error_word() {
   return g_error_ptr[dev];
 }
 
+int check_current_device(const char* fn, std::initializer_list<const void*> ptrs) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(SPECKV_ECUDA, "%s: no current CUDA device", fn);
+  for (const void* p : ptrs) {
+    if (p == nullptr) continue;
+    cudaPointerAttributes at;
+    const cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+      cudaGetLastError();  // not sticky: clear it so the next launch check does not see it
+      return fail(SPECKV_EINVAL, "%s: operand %p is not an address CUDA knows (%s)", fn, p, cudaGetErrorString(e));
+    }
+    if (at.type == cudaMemoryTypeDevice && at.device != dev)
+      return fail(SPECKV_EINVAL, "%s: operand %p lives on cuda:%d but the current device is cuda:%d", fn, p,
+                  at.device, dev);
+    if (at.type == cudaMemoryTypeUnregistered)
+      return fail(SPECKV_EINVAL, "%s: operand %p is host memory the GPU cannot reach", fn, p);
+  }
+  return SPECKV_OK;
+}
+
 }  // namespace speckv
 
 extern "C" int speckv_version(void) { return 100; }

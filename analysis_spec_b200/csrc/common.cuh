@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <initializer_list>
 #include <stdint.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -21,6 +22,11 @@ int check_launch(const char* what);
 
 // Device address of the library's error word on the current device.
 unsigned long long* device_error_word();
+
+// Kernels launch on the current GPU: returns SPECKV_EINVAL (with message) when one of
+// `ptrs` is device memory of another GPU or plain (unregistered) host memory. Null
+// entries, pinned host memory and managed memory pass. One driver query per pointer.
+int check_current_device(const char* fn, std::initializer_list<const void*> ptrs);
 
 // ---- device error word --------------------------------------------------------
 

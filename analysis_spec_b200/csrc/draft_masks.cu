@@ -131,6 +131,8 @@ extern "C" int speckv_causal_mask(void* mask, int32_t dtype, int64_t batch, int6
   if (st) return st;
   if (past < 0) return fail(SPECKV_EINVAL, "%s: negative past", fn);
   if (batch * query == 0 || columns == 0) return SPECKV_OK;
+  st = check_current_device(fn, {mask, pad, bits, first_col});
+  if (st) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   st = check_bits(fn, batch, columns, bits, row_words, first_col, s);
   if (st) return st;
@@ -150,6 +152,8 @@ extern "C" int speckv_expansion_mask(void* mask, int32_t dtype, int64_t batch, i
   if (st) return st;
   if (batch * query == 0 || columns == 0) return SPECKV_OK;
   if (seen == nullptr) return fail(SPECKV_EINVAL, "%s: null seen positions", fn);
+  st = check_current_device(fn, {mask, seen, pad, bits, first_col});
+  if (st) return st;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -175,6 +175,8 @@ extern "C" int speckv_history_append(int32_t fields, void* const* pools, const i
   }
   if (t.total == 0) return SPECKV_OK;
   if (any_pool && owners == nullptr) return fail(SPECKV_EINVAL, "%s: null owners", fn);
+  const int dst = check_current_device(fn, {t.f[0].src, t.f[0].pool, t.f[0].gathered, owners});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   history_append_kernel<<<grid_for(t.total), kHistThreads, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -190,6 +192,8 @@ extern "C" int speckv_history_pack(void* dst, const void* pool, int64_t pool_row
   if (rows == 0 || max_length == 0) return SPECKV_OK;
   if (!dst || !pool || !offsets) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
   if (rows > 65535) return fail(SPECKV_ENOSUPPORT, "%s: more than 65535 rows", fn);
+  const int dst_ok = check_current_device(fn, {dst, pool, offsets});
+  if (dst_ok) return dst_ok;
   const long long vals[5] = {row_bytes, pool_row_stride, pool_pos_stride, (long long)(uintptr_t)dst,
                              (long long)(uintptr_t)pool};
   const int vec = pick_vec(vals, 5);

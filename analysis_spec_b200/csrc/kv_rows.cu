@@ -471,6 +471,7 @@ int pool_vec(void* const* kp, void* const* vp, int layers, long long row_bytes) 
 
 // A validated, packed launch: host work before the enqueue is done once, at preparation.
 struct LaunchPlan {
+  int device = -1;  // the GPU the plan was prepared on (its pointers live there)
   virtual ~LaunchPlan() = default;
   virtual int launch(cudaStream_t s) const = 0;
 };
@@ -574,7 +575,12 @@ extern "C" int speckv_append_rows_prepare(void* const* key_pools, void* const* v
 
 extern "C" int speckv_plan_launch(const void* plan, void* stream) {
   if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_plan_launch: null plan");
-  return static_cast<const LaunchPlan*>(plan)->launch(static_cast<cudaStream_t>(stream));
+  const LaunchPlan* p = static_cast<const LaunchPlan*>(plan);
+  int dev = -1;
+  if (p->device >= 0 && (cudaGetDevice(&dev) != cudaSuccess || dev != p->device))
+    return fail(SPECKV_EINVAL, "speckv_plan_launch: plan prepared on cuda:%d, current device is cuda:%d", p->device,
+                dev);
+  return p->launch(static_cast<cudaStream_t>(stream));
 }
 
 extern "C" void speckv_plan_release(void* plan) { delete static_cast<LaunchPlan*>(plan); }
@@ -624,7 +630,10 @@ int prepare_append(void* const* key_pools, void* const* value_pools, const void*
   const long long nvec = row_bytes / vec;
   const long long total = batch * heads * rows * nvec;
   if (!fits_u31(total)) return fail(SPECKV_ENOSUPPORT, "%s: %lld vectors per tensor exceeds 2^31", fn, total);
+  st = check_current_device(fn, {key_pools[0], value_pools[0], key_srcs[0], value_srcs[0], row_table});
+  if (st) return st;
   AppendPlan* plan = new AppendPlan();
+  cudaGetDevice(&plan->device);
   PoolTable& dst = plan->dst;
   fill_pools(dst, key_pools, value_pools, layers);
   AppendGeom& g = plan->g;
@@ -680,6 +689,8 @@ extern "C" int speckv_compact_suffix(void* const* key_pools, void* const* value_
                 (long long)past, (long long)width, (long long)length, (long long)capacity);
   if (batch == 0 || extension == width) return SPECKV_OK;
   if (chosen == nullptr) return fail(SPECKV_EINVAL, "%s: null chosen", fn);
+  st = check_current_device(fn, {key_pools[0], value_pools[0], chosen, row_table});
+  if (st) return st;
   const long long row_bytes = dim * elem_bytes;
   const int vec = pool_vec(key_pools, value_pools, layers, row_bytes);
   const long long nvec = row_bytes / vec;
@@ -811,9 +822,15 @@ int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t lay
   const long long position_blocks = positions != nullptr ? (batch + kThreads / 32 - 1) / (kThreads / 32) : 0;
   if (!fits_u31(groups) || !fits_u31(compact_blocks + position_blocks) || !fits_u31(batch * (layers != 0 ? heads : 1)))
     return fail(SPECKV_ENOSUPPORT, "%s: problem too large for 32-bit indexing", fn);
+  const void* k0 = layers != 0 ? key_pools[0] : nullptr;
+  const void* v0 = layers != 0 ? value_pools[0] : nullptr;
+  const int dst = check_current_device(fn, {k0, v0, packet, chosen, row_table, pad_rows, owners, pad_live,
+                                            newly_padded, positions, past_positions});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   CommitPlan* plan = new CommitPlan();
+  cudaGetDevice(&plan->device);
   PoolTable& pools = plan->pools;
   if (layers != 0) fill_pools(pools, key_pools, value_pools, layers);
   RoundGeom& g = plan->g;
@@ -876,6 +893,8 @@ extern "C" int speckv_remap_rows(void* const* key_pools, void* const* value_pool
   if (length > capacity) return fail(SPECKV_EINVAL, "%s: length exceeds capacity", fn);
   if (new_batch == 0 || length == 0) return SPECKV_OK;
   if (indices == nullptr) return fail(SPECKV_EINVAL, "%s: null indices", fn);
+  st = check_current_device(fn, {key_pools[0], value_pools[0], indices, scratch});
+  if (st) return st;
   if (!fits_u31(batch_capacity) || !fits_u31(length)) return fail(SPECKV_ENOSUPPORT, "%s: sizes exceed 2^31", fn);
   const long long row_bytes = dim * elem_bytes;
   unsigned long long* err = device_error_word();
@@ -964,6 +983,8 @@ extern "C" int speckv_move_rows(void* const* key_pools, void* const* value_pools
   if (length > capacity) return fail(SPECKV_EINVAL, "%s: length exceeds capacity", fn);
   if (count == 0 || length == 0) return SPECKV_OK;
   if (sources == nullptr || destinations == nullptr) return fail(SPECKV_EINVAL, "%s: null index list", fn);
+  st = check_current_device(fn, {key_pools[0], value_pools[0], sources, destinations});
+  if (st) return st;
   if (!fits_u31(batch_capacity)) return fail(SPECKV_ENOSUPPORT, "%s: batch capacity exceeds 2^31", fn);
   const long long row_bytes = dim * elem_bytes;
   const int vec = pool_vec(key_pools, value_pools, layers, row_bytes);

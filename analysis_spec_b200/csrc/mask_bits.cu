@@ -72,6 +72,8 @@ extern "C" int speckv_mask_bits(const void* mask, int32_t dtype, int64_t batch, 
   if (batch * rows == 0) return SPECKV_OK;
   if (!mask || !mask_strides || !bits || !first_col || !nonbinary) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
   if (batch * rows > 0x7fffffffll) return fail(SPECKV_ENOSUPPORT, "%s: too many mask rows", fn);
+  const int dst = check_current_device(fn, {mask, bits, first_col, nonbinary});
+  if (dst) return dst;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // first_col starts above any column (atomicMin), the flag at 0
   if (cudaMemsetAsync(first_col, 0x7f, (size_t)batch * sizeof(int32_t), s) != cudaSuccess ||

@@ -121,20 +121,28 @@ extern "C" int speckv_remap_rows_static(void* const* key_pools, void* const* val
     return fail(SPECKV_EINVAL, "%s: new batch %lld exceeds batch capacity %lld", fn, (long long)new_batch,
                 (long long)batch_capacity);
   if (length > capacity) return fail(SPECKV_EINVAL, "%s: length exceeds capacity", fn);
+  // Every size below stays under 2^31, so the byte products that follow cannot overflow
+  // (an overflowed product could pass the scratch check and give a chunk <= 0).
+  if (!fits_u31(new_batch) || !fits_u31(batch_capacity) || !fits_u31(heads) || !fits_u31(dim) ||
+      !fits_u31(capacity) || !fits_u31(length) || !fits_u31(dim * elem_bytes))
+    return fail(SPECKV_EINVAL, "%s: a size is 2^31 or more", fn);
   const long long row_bytes = dim * elem_bytes;
   // K and V rows of one position for every output row must fit; longer prefixes
-  // are processed in position chunks.
-  const long long per_position = 2 * new_batch * heads * row_bytes;
-  if (per_position > (long long)SPECKV_REMAP_STATIC_SCRATCH_BYTES)
+  // are processed in position chunks. Compared by division first, so that the
+  // product below is only formed once it is known to fit.
+  const long long rows_fit = (long long)SPECKV_REMAP_STATIC_SCRATCH_BYTES / (2 * row_bytes);
+  if (new_batch > 0 && heads > rows_fit / new_batch)
     return fail(SPECKV_EINVAL,
-                "%s: %lld rows x %lld heads x %lld-byte rows need %lld scratch bytes per position, above the "
-                "%lld-byte static scratch; use speckv_remap_rows with caller scratch",
-                fn, (long long)new_batch, (long long)heads, row_bytes, per_position,
-                (long long)SPECKV_REMAP_STATIC_SCRATCH_BYTES);
+                "%s: %lld rows x %lld heads x %lld-byte rows (K and V) exceed the %lld-byte static scratch per "
+                "position; use speckv_remap_rows with caller scratch",
+                fn, (long long)new_batch, (long long)heads, row_bytes, (long long)SPECKV_REMAP_STATIC_SCRATCH_BYTES);
+  const long long per_position = 2 * new_batch * heads * row_bytes;
   if (new_batch == 0 || length == 0) return SPECKV_OK;
   if (indices == nullptr) return fail(SPECKV_EINVAL, "%s: null indices", fn);
+  int st = check_current_device(fn, {key_pools[0], value_pools[0], indices});
+  if (st) return st;
   unsigned char* scratch = nullptr;
-  int st = scratch_address(&scratch);
+  st = scratch_address(&scratch);
   if (st) return st;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);

@@ -401,6 +401,8 @@ extern "C" int speckv_trace_path(const int64_t* parents, const int64_t* tokens, 
   if (batch == 0) return SPECKV_OK;
   if (!parents || !tokens || !contexts || !samples || !lengths || (width > 0 && (!out_tokens || !out_indices || !out_contexts)))
     return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  const int dst = check_current_device(fn, {samples, lengths});
+  if (dst) return dst;
   const int threads = 128;
   const long long blocks = (batch * 32 + threads - 1) / threads;
   trace_path_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -420,6 +422,8 @@ extern "C" int speckv_pack_tree(const int64_t* full_parents, const int64_t* full
       (packed_count > 0 && !chosen))
     return fail(SPECKV_EINVAL, "%s: null pointer", fn);
   if (full_count + 1 > 50000) return fail(SPECKV_ENOSUPPORT, "%s: %lld draft nodes too many", fn, (long long)full_count);
+  const int dst = check_current_device(fn, {full_parents, out_parents});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   const size_t smem = (size_t)(full_count + 1) * sizeof(int);
@@ -437,6 +441,8 @@ static int launch_pad(const char* fn, PadArgs& a, void* stream) {
   if (a.capacity > (1 << 20)) return fail(SPECKV_ENOSUPPORT, "%s: capacity %lld too large", fn, a.capacity);
   if (!a.tokens || !a.indices || !a.lengths || !a.ot || !a.oi || !a.om || !a.last)
     return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  const int dst = check_current_device(fn, {a.tokens, a.ot, a.packet});
+  if (dst) return dst;
   const size_t smem = (size_t)a.capacity * sizeof(int);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (smem > 48 * 1024) cudaFuncSetAttribute(pad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -487,6 +493,8 @@ extern "C" int speckv_tree_mask(const int64_t* parents, int64_t batch, int64_t r
   if (batch == 0) return SPECKV_OK;
   if (!parents || !mask) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
   if (batch > 65535) return fail(SPECKV_ENOSUPPORT, "%s: batch above 65535", fn);
+  const int dst = check_current_device(fn, {parents, mask, pad});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   const long long cols = past + rows;
@@ -510,6 +518,8 @@ extern "C" int speckv_tree_mask_bits(const int64_t* parents, int64_t batch, int6
   if (batch == 0) return SPECKV_OK;
   if (!parents || !bits || !first_col) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
   if (batch > 65535) return fail(SPECKV_ENOSUPPORT, "%s: batch above 65535", fn);
+  const int dst = check_current_device(fn, {parents, bits, first_col, pad});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -544,6 +554,8 @@ extern "C" int speckv_position_update(uint8_t* pad_rows, int64_t pad_rows_stride
     return fail(SPECKV_EINVAL, "%s: padding rows need owners and past + width <= row stride", fn);
   if (pad_live != nullptr && past + width > pad_live_stride)
     return fail(SPECKV_EINVAL, "%s: past + width exceeds live padding row stride", fn);
+  const int dst = check_current_device(fn, {newly_padded, positions, pad_rows});
+  if (dst) return dst;
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
   const int threads = 128;

@@ -19,6 +19,11 @@
  * Index inputs (int64) that address cache rows are bounds-checked on the
  * device: an out-of-range entry is skipped and recorded in a device-side error
  * word that speckv_device_error() reads back and clears. Kernels never trap.
+ *
+ * Kernels launch on the CURRENT device: an operand that is device memory of
+ * another GPU, or plain host memory, is refused with SPECKV_EINVAL before any
+ * launch (checked with the driver's pointer attributes). A prepared plan
+ * launches only while the device it was prepared on is current.
  */
 #ifndef SPECKV_H
 #define SPECKV_H
@@ -368,7 +373,11 @@ int speckv_position_update(uint8_t* pad_rows, int64_t pad_rows_stride, int64_t p
 /* ---- tree-verify attention -------------------------------------------- */
 
 /* GQA attention of `rows` tree queries over kv_len cached positions with an
- * additive mask, without materialising repeated K/V:
+ * additive mask, without materialising repeated K/V.
+ * Head dim 128 in bf16 / fp16 runs on the tcgen05 tensor-core kernels only: a
+ * view of that shape with a base or stride that is not 16-byte aligned is
+ * refused with SPECKV_ENOSUPPORT (no silent slower path). Other head dims and
+ * fp32 run on a CUDA-core kernel. speckv_attention_launches counts both.
  *   out[b][r][hq][:] = softmax_c(q[b][hq][r] . k[b][hq / g][c] * scale + mask[b][0][r][c]) v[b][hq/g][c]
  * g = q_heads / kv_heads. q/k/v element strides are given as (b, h, t) with unit
  * stride on dim; mask is (batch, 1, rows, kv_len) contiguous in `mask_dtype`
@@ -416,6 +425,23 @@ int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
                                void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
                                int64_t rows, int64_t kv_len, int64_t dim, float scale,
                                int32_t dtype, const int64_t* row_table, int64_t kv_batch, void* stream);
+
+/* Launches issued since the library was loaded by speckv_tree_attention /
+ * speckv_tree_attention_bits calls, per kernel family: *tensor_core the tcgen05
+ * kernels, *cuda_core the CUDA-core kernel (other head dims, fp32). Replays of a
+ * captured CUDA graph are not calls and are not counted. No reference
+ * counterpart (the reference dispatches inside torch's SDPA). */
+int speckv_attention_launches(int64_t* tensor_core, int64_t* cuda_core);
+
+/* Test hook of the tensor-core attention kernels on the current device
+ * (synchronous): every bounded wait inside them gives up after wait_limit_ns
+ * (0 = the default of 2 s) and records SPECKV_DERR_TIMEOUT with the wait site;
+ * withhold_q_arrival = 1 makes CTA 0 of the visibility-bits kernel withhold the
+ * arrival of its first Q tile, so that the MMA warp's wait for it runs out with
+ * no copy or MMA in flight and the kernel unwinds. Lets a test check the
+ * timeout path without a GPU fault; keep both 0 otherwise. No reference
+ * counterpart (the reference's kernels have no bounded waits). */
+int speckv_attention_test_hooks(int64_t wait_limit_ns, int32_t withhold_q_arrival);
 
 #ifdef __cplusplus
 }

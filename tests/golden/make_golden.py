@@ -2,7 +2,9 @@
 
 Run from the repository root with the reference checkout available:
 
-    python tests/golden/make_golden.py [/path/to/analysis_spec]
+    python tests/golden/make_golden.py /path/to/analysis_spec
+
+(the path of the reference checkout is required).
 
 The reference's torch (CPU) branch and its Triton kernels (executed on CPU
 tensors by the Triton interpreter, TRITON_INTERPRET=1) produce the expected
@@ -25,7 +27,9 @@ os.environ['TRITON_INTERPRET'] = '1'  # must precede the first triton import
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference').resolve()
+if len(sys.argv) < 2:
+    sys.exit('usage: python tests/golden/make_golden.py /path/to/analysis_spec (the reference checkout)')
+REF = Path(sys.argv[1]).resolve()
 sys.path.insert(0, str(REF))
 OUT = Path(__file__).resolve().parent
 

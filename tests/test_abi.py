@@ -83,3 +83,25 @@ def test_prepared_launch_host_side(lib):
     plan()
     plan()  # a plan can be launched again
     del plan
+
+
+def test_static_remap_refuses_sizes_that_would_overflow(lib):
+    """Sizes whose byte products overflow 64 bits are refused before any CUDA call."""
+    pools = (ctypes.c_void_p * 1)(16)  # never dereferenced: the size checks come first
+    idx = ctypes.c_void_p(16)
+    with pytest.raises(_lib.SpecKVError, match='2\\^31 or more'):
+        _lib.call('speckv_remap_rows_static', pools, pools, 1, idx, 1 << 31, 1 << 31, 2, 128, 8, 8, 2, None)
+    # each size below 2^31, but 2 * rows * heads * row bytes is about 2^84
+    with pytest.raises(_lib.SpecKVError, match='static scratch'):
+        _lib.call('speckv_remap_rows_static', pools, pools, 1, idx, 1 << 30, 1 << 30, 1 << 30, 1 << 20, 8, 8, 8,
+                  None)
+
+
+def test_attention_counters_and_hook_arguments(lib):
+    tc, cc = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    _lib.call('speckv_attention_launches', ctypes.byref(tc), ctypes.byref(cc))
+    assert tc.value >= 0 and cc.value >= 0
+    with pytest.raises(_lib.SpecKVError, match='0 / 1 switch'):
+        _lib.call('speckv_attention_test_hooks', -1, 0)
+    with pytest.raises(_lib.SpecKVError, match='0 / 1 switch'):
+        _lib.call('speckv_attention_test_hooks', 0, 2)
