@@ -627,7 +627,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // longest-first list of work items (sequence b, KV head, pair of 128-row tiles);
 // both row tiles of an item consume every K/V tile it loads.
 //
-//   warp 0      TMA producer: K and V tiles in separate 2-stage rings
+// Row packing: a 128-row tile holds q = floor(128 / g) whole tree rows, tile row
+// s = (r - q * tile) * g + j for tree row r and query head j of the KV group, so
+// that one 4-D TMA box (64 dims x g heads x q rows) fetches it from the strided
+// projection; rows q * g .. 127 stay zero (they are never written).
+//
+//   warp 0      TMA producer: the Q tiles of the next item (as soon as the last
+//               S MMA of the current item has read the Q buffer), then K and V
+//               tiles in separate 2-stage rings
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
 //               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
 //               warpgroup works while the tensor pipe serves the other tile
@@ -645,8 +652,9 @@ constexpr int kThreads2 = 384;
 // to kRegsLow, the two softmax warpgroups rise to kRegsHigh. The block is launched
 // with kRegsLaunch per thread (the host checks the compiled count), and
 // 128 * kRegsLow + 256 * kRegsHigh == 384 * kRegsLaunch, so every increase is
-// covered by the decrease.
-constexpr int kRegsLaunch = 168, kRegsLow = 136, kRegsHigh = 184;
+// covered by the decrease. 88 / 208 leaves the softmax loop (128 scores per thread)
+// almost free of spills; below 88 the producer and MMA warps spill instead.
+constexpr int kRegsLaunch = 168, kRegsLow = 88, kRegsHigh = 208;
 static_assert(128 * kRegsLow + 256 * kRegsHigh == kThreads2 * kRegsLaunch, "register split must balance");
 constexpr int kMaxSortB = 1024;
 constexpr uint32_t Q2_OFF = 0;                    // Q tile t at Q2_OFF + t * kTileBytes
@@ -660,7 +668,7 @@ __host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u;
 __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
 
 enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
-       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19 };
+       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19, C_Q_EMPTY = 20, C_O_READ = 22 };
 
 // Warp-wide forms: every lane runs the same code (the operands stay warp-uniform) and
 // one elected lane, always lane 0 with the full mask, issues the instruction; the
@@ -718,6 +726,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
       "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
+}
+
+// 32 bytes to global memory in one instruction (address 32-byte aligned)
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
 }
 
 // (a.x * b.x + c.x, a.y * b.y + c.y) and (a.x + b.x, a.y + b.y) on the packed f32x2 pipe
@@ -783,13 +798,14 @@ struct Item {
 // softmax warpgroups serve the one Q tile and take alternate key tiles (warpgroup w the
 // tiles i with i % 2 == w); S_w of tile i and the P.V of tile i - 1 are issued in turn,
 // so the K and V rings are consumed in order. Warpgroup 1 hands its running max and sum
-// to warpgroup 0 through shared memory (C_XCHG, a bounded wait), which merges O0 and O1.
+// to warpgroup 0 through shared memory (C_XCHG, a bounded wait), which merges O0 and O1
+// and then signals C_O_READ: the next item's first P.V waits for it.
 // TABLE: the K/V rows of sequence b come from a.row_table[b] (a separate instantiation, so
 // the table-free kernel carries no trace of it).
 template <typename T, bool SPLIT, bool TABLE>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                     const Sm100Args a, const KvRows kvr) {
+                     const __grid_constant__ CUtensorMap tmq, const Sm100Args a, const KvRows kvr) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -801,8 +817,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
   int* order = reinterpret_cast<int*>(smem + ORD2_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_rows = a.group * a.rows;
-  const int pairs = (total_rows + 2 * BM - 1) / (2 * BM);
+  const int qrows = BM / a.group;                        // whole tree rows per 128-row tile
+  const int mtiles = (a.rows + qrows - 1) / qrows;       // row tiles per (sequence, KV head)
+  const int pairs = SPLIT ? 1 : (mtiles + 1) / 2;
   const int per_b = a.kv_heads * pairs;
   const int n_items = a.batch * per_b;
   const int n_tiles_all = (a.kv_len + BN - 1) / BN;
@@ -821,11 +838,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mbar_init(bar(C_V_EMPTY + i), 1);
       mbar_init(bar(C_S_FULL + i), 1);
       mbar_init(bar(C_O_FINAL + i), 1);
-      mbar_init(bar(C_Q_FULL + i), 128);
+      mbar_init(bar(C_Q_FULL + i), 1);
+      mbar_init(bar(C_Q_EMPTY + i), 1);
       mbar_init(bar(C_P_FULL + i), 128);
     }
     mbar_init(bar(C_DRAIN), 1);
     mbar_init(bar(C_XCHG), 128);
+    mbar_init(bar(C_O_READ), 128);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -834,6 +853,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // Rows qrows * g .. 127 of both Q tiles are never written by the Q loads: zero them once
+  // (generic-proxy stores, made visible to the tensor cores' async proxy).
+  {
+    const int pad_chunks = (BM - qrows * a.group) * 16;
+    for (int i = threadIdx.x; i < 2 * pad_chunks; i += kThreads2) {
+      const int tile = i / pad_chunks, rem = i % pad_chunks;
+      *reinterpret_cast<uint4*>(smem + Q2_OFF + tile * kTileBytes + sw_chunk(qrows * a.group + rem / 16, rem % 16)) =
+          make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async();
   }
   // longest sequences first: order[rank] = b, ties by index
   if (sorted) {
@@ -869,10 +899,29 @@ __global__ void __launch_bounds__(kThreads2, 1)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
       int cnt = 0, issued_k = 0, issued_v = 0;
+      int qc[2] = {0, 0};           // Q tiles requested per row tile
+      bool q_issued[2] = {false, false};  // the latest request was sent (not withheld)
+      const bool withhold = blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0;
+      const uint32_t q_bytes = 2u * 128u * (uint32_t)(qrows * a.group);  // two 64-dim halves of q * g rows
       bool ok = true;
       Item it;
       for (int k = 0; ok && item_at(k, it); ++k) {
+        // Q tiles of the item: each buffer is free once the previous item's last S MMA has read it
+        const int ntq = (SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2;
+        for (int t = 0; t < ntq; ++t) {
+          if (qc[t] >= 1 && !mbar_wait(bar(C_Q_EMPTY + t), (qc[t] - 1) & 1, abort_flag, a.err, 20)) { ok = false; break; }
+          ++qc[t];
+          q_issued[t] = !(withhold && k == 0 && t == 0);  // test hook: this tile never arrives
+          if (!q_issued[t]) continue;
+          const uint32_t qd = sbase + Q2_OFF + t * kTileBytes;
+          const int r0 = SPLIT ? 0 : (it.pair * 2 + t) * qrows;
+          mbar_expect_tx(bar(C_Q_FULL + t), q_bytes);
+          tma_load_4d(qd, &tmq, bar(C_Q_FULL + t), 0, it.kvh * a.group, r0, it.b);
+          tma_load_4d(qd + kTileHalf, &tmq, bar(C_Q_FULL + t), 64, it.kvh * a.group, r0, it.b);
+        }
+        if (!ok) break;
         const int t0 = first_tile(it.b);
         int kb = it.b;  // K/V row of the sequence: through the row table when there is one
         if (TABLE) {
@@ -905,6 +954,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
       // these phases completed long ago and the waits return at once.
       for (int q = issued_k - 2 < 0 ? 0 : issued_k - 2; q < issued_k; ++q) drain_wait(bar(C_K_FULL + (q & 1)), (q >> 1) & 1);
       for (int q = issued_v - 2 < 0 ? 0 : issued_v - 2; q < issued_v; ++q) drain_wait(bar(C_V_FULL + (q & 1)), (q >> 1) & 1);
+      for (int t = 0; t < 2; ++t)
+        if (qc[t] >= 1 && q_issued[t]) drain_wait(bar(C_Q_FULL + t), (qc[t] - 1) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (whole warp, lane 0 issues) ----------------
@@ -963,6 +1014,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
           const int n = n_tiles_all - first_tile(it.b);
           ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
           tc_fence_after();
+          // O0 and O1 of the previous item must be read (merged) before this item's first P.V
+          bool o_busy = ic[0] >= 1;
+          auto o_free = [&]() -> bool {
+            if (!o_busy) return true;
+            o_busy = false;
+            if (!wait(C_O_READ, (ic[0] - 1) & 1, 31)) return false;
+            tc_fence_after();
+            return true;
+          };
           int prev_stage = 0;
           for (int i = 0; ok && i < n; ++i, ++cnt) {
             const int s = cnt & 1, w = i & 1;
@@ -970,10 +1030,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
             tc_fence_after();
             issue_s(w, s, 0);
             tc_commit_w(bar(C_K_EMPTY + s));
+            if (i == n - 1) tc_commit_w(bar(C_Q_EMPTY + 0));  // the last S MMA has read Q
             if (i > 0) {  // P.V of the previous tile, the other warpgroup's
               if (!wait(C_V_FULL + prev_stage, ((cnt - 1) >> 1) & 1, 27)) { ok = false; break; }
               tc_fence_after();
-              if (!issue_pv(1 - w, prev_stage, i - 1 < 2)) { ok = false; break; }
+              if (!o_free() || !issue_pv(1 - w, prev_stage, i - 1 < 2)) { ok = false; break; }
               tc_commit_w(bar(C_V_EMPTY + prev_stage));
             }
             prev_stage = s;
@@ -983,7 +1044,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
               ok = false;
             } else {
               tc_fence_after();
-              if (issue_pv((n - 1) & 1, prev_stage, n - 1 < 2)) tc_commit_w(bar(C_V_EMPTY + prev_stage));
+              if (o_free() && issue_pv((n - 1) & 1, prev_stage, n - 1 < 2)) tc_commit_w(bar(C_V_EMPTY + prev_stage));
               else ok = false;
             }
           }
@@ -994,7 +1055,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           ++ic[1];
           continue;
         }
-        const bool act1 = it.pair * 2 * BM + BM < total_rows;
+        const bool act1 = it.pair * 2 + 1 < mtiles;
         const int n = n_tiles_all - first_tile(it.b);
         ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
         if (ok && act1) ok = wait(C_Q_FULL + 1, ic[1] & 1, 25);
@@ -1011,10 +1072,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
           if (act1) issue_s(1, s, 1);
           tc_commit_w(bar(C_K_EMPTY + s));
+          if (i == n - 1) {  // the last S MMAs have read the Q tiles: the next item's Q may load
+            tc_commit_w(bar(C_Q_EMPTY + 0));
+            if (act1) tc_commit_w(bar(C_Q_EMPTY + 1));
+          }
           if (!wait(C_V_FULL + s, (cnt >> 1) & 1, 27)) { ok = false; break; }
           tc_fence_after();
           if (!issue_pv(0, s, i == 0)) { ok = false; break; }
           if (!act1) tc_commit_w(bar(C_V_EMPTY + s));
+          if (i == n - 1) tc_commit_w(bar(C_O_FINAL + 0));  // O0 is final: its epilogue need not wait for P1
           prev_stage = s;
         }
         if (ok && act1) {
@@ -1022,7 +1088,6 @@ __global__ void __launch_bounds__(kThreads2, 1)
           else ok = false;
         }
         if (!ok) break;
-        tc_commit_w(bar(C_O_FINAL + 0));
         ++ic[0];
         if (act1) {
           tc_commit_w(bar(C_O_FINAL + 1));
@@ -1047,42 +1112,27 @@ __global__ void __launch_bounds__(kThreads2, 1)
       bool valid;
       int r, hq;
     };
+    // tile row -> (tree row, query head): the packing of the Q tensor map's boxes
     auto row_map = [&](const Item& x) {
       RowMap m;
-      const int grow = SPLIT ? row : x.pair * 2 * BM + t * BM + row;
-      m.valid = grow < total_rows;
-      m.r = m.valid ? grow / a.group : 0;
-      m.hq = x.kvh * a.group + (m.valid ? grow % a.group : 0);
+      const int tile = SPLIT ? 0 : x.pair * 2 + t;
+      const int rr = tile * qrows + row / a.group;
+      m.valid = row < qrows * a.group && rr < a.rows;
+      m.r = m.valid ? rr : 0;
+      m.hq = x.kvh * a.group + (m.valid ? row % a.group : 0);
       return m;
-    };
-    // Q rows of item x -> swizzled shared tile t (zeros for padding rows), then Q_FULL
-    // (withheld when the test hook asks it of this CTA's first item)
-    auto write_q = [&](const Item& x, bool withhold) {
-      const RowMap m = row_map(x);
-      const T* qrow = static_cast<const T*>(a.q) + (long long)x.b * a.qs0 + (long long)m.hq * a.qs1 +
-                      (long long)m.r * a.qs2;
-      uint8_t* qt = smem + Q2_OFF + (SPLIT ? 0 : t) * kTileBytes;
-      uint4 v[16];  // all loads in flight before the first shared-memory store
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc)
-        v[cc] = m.valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + cc) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) *reinterpret_cast<uint4*>(qt + sw_chunk(row, cc)) = v[cc];
-      fence_proxy_async();
-      if (!withhold) mbar_arrive(bar(C_Q_FULL + (SPLIT ? 0 : t)));
     };
     auto next_item = [&](int& kk, Item& nx) -> bool {
       for (;; ++kk) {
         if (!item_at(kk, nx)) return false;
-        if (SPLIT || t == 0 || nx.pair * 2 * BM + BM < total_rows) return true;
+        if (SPLIT || t == 0 || nx.pair * 2 + 1 < mtiles) return true;
       }
     };
+    const bool out32 = (reinterpret_cast<uintptr_t>(a.out) & 31u) == 0;  // 32-byte output stores
     int sc = 0, ic = 0, k = 0;
     bool ok = true;
     Item it;
     bool have = next_item(k, it);
-    if (have && (!SPLIT || t == 0))
-      write_q(it, blockIdx.x == 0 && t == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0);
     const int i_first = SPLIT ? t : 0, i_step = SPLIT ? 2 : 1;  // this warpgroup's key tiles
     while (have) {
       const int t0 = first_tile(it.b);
@@ -1161,13 +1211,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
         l_run = l_run * corr + ((s01.x + s01.y) + (s23.x + s23.y));
       }
       if (!ok) break;
-      // The last S_t of this item has completed, so Q tile t is free: stage the next
-      // item now so its first S MMA can overlap this item's epilogue.
       Item nx;
       int kn = k + 1;
       const bool have_next = next_item(kn, nx);
-      // (SPLIT: warpgroup 1's last S may still read Q tile 0; the next Q waits for the merge)
-      if (have_next && !SPLIT) write_q(nx, false);
       ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
@@ -1214,7 +1260,15 @@ __global__ void __launch_bounds__(kThreads2, 1)
             for (int j = 0; j < 32; ++j) o[h * 32 + j] = o[h * 32 + j] * c0 + (use1 ? o1[j] * c1 : 0.f);
           }
         }
-        if (m.valid) {
+        if (m.valid && out32) {  // whole 32-byte sectors: half the store transactions
+#pragma unroll
+          for (int j = 0; j < 64; j += 16) {
+            uint32_t w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w[e] = pack2<T>(o[j + 2 * e] * inv, o[j + 2 * e + 1] * inv);
+            st_global_v8(orow + cc * 64 + j, w);
+          }
+        } else if (m.valid) {
 #pragma unroll
           for (int j = 0; j < 64; j += 8) {
             uint4 v;
@@ -1227,7 +1281,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
       }
       tc_fence_before();
-      if (SPLIT && have_next) write_q(nx, false);  // O0 and O1 are read: the next item may start
+      if (SPLIT) mbar_arrive(bar(C_O_READ));  // O0 and O1 are read: the next item's P.V may start
       it = nx;
       k = kn;
       have = have_next;
@@ -1257,52 +1311,71 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Encoded maps of the views seen last on this thread: the verify loop hands every layer's
-// K/V cache views again each round, so their maps are encoded once.
-struct KvMapEntry {
+// K/V cache views and query projections again each round, so their maps are encoded once.
+struct MapEntry {
   const void* base;
-  long long st[3], batch, heads, len;
-  int dtype;
+  long long dims[3], strides[3];
+  int box1, box2, dtype;
   CUtensorMap map;
 };
-constexpr int kKvMapCache = 256;
+constexpr int kMapCache = 256;
 
-// 4-D map over a (batch, heads, len, 128) strided view: dims (d, len, heads, batch).
-bool make_kv_map(CUtensorMap* map, const void* base, const long long* st, long long batch, long long heads,
-                 long long len, int dtype) {
-  thread_local KvMapEntry cache[kKvMapCache];
+// 4-D map with a 128-element (head dim) innermost dimension, 128-byte swizzle and a box of
+// (64, box1, box2, 1): dims[i] / strides[i] (elements) are the three outer dimensions.
+bool make_map(CUtensorMap* map, const void* base, const long long* dims, const long long* strides, int box1,
+              int box2, int dtype) {
+  thread_local MapEntry cache[kMapCache];
   thread_local int used = 0, next = 0;
   for (int i = 0; i < used; ++i) {
-    const KvMapEntry& e = cache[i];
-    if (e.base == base && e.st[0] == st[0] && e.st[1] == st[1] && e.st[2] == st[2] && e.batch == batch &&
-        e.heads == heads && e.len == len && e.dtype == dtype) {
+    const MapEntry& e = cache[i];
+    if (e.base == base && e.dims[0] == dims[0] && e.dims[1] == dims[1] && e.dims[2] == dims[2] &&
+        e.strides[0] == strides[0] && e.strides[1] == strides[1] && e.strides[2] == strides[2] &&
+        e.box1 == box1 && e.box2 == box2 && e.dtype == dtype) {
       *map = e.map;
       return true;
     }
   }
   auto fn = encode_fn();
   if (fn == nullptr) return false;
-  const cuuint64_t dims[4] = {(cuuint64_t)HD, (cuuint64_t)len, (cuuint64_t)heads, (cuuint64_t)batch};
-  const cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
-  const cuuint32_t box[4] = {64, BN, 1, 1};
+  const cuuint64_t gdims[4] = {(cuuint64_t)HD, (cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2]};
+  const cuuint64_t gstrides[3] = {(cuuint64_t)strides[0] * 2, (cuuint64_t)strides[1] * 2,
+                                  (cuuint64_t)strides[2] * 2};
+  const cuuint32_t box[4] = {64, (cuuint32_t)box1, (cuuint32_t)box2, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult res = fn(map, dtype == SPECKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                    4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    4, const_cast<void*>(base), gdims, gstrides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (res != CUDA_SUCCESS) return false;
-  KvMapEntry& e = cache[next];
+  MapEntry& e = cache[next];
   e.base = base;
-  e.st[0] = st[0];
-  e.st[1] = st[1];
-  e.st[2] = st[2];
-  e.batch = batch;
-  e.heads = heads;
-  e.len = len;
+  for (int i = 0; i < 3; ++i) {
+    e.dims[i] = dims[i];
+    e.strides[i] = strides[i];
+  }
+  e.box1 = box1;
+  e.box2 = box2;
   e.dtype = dtype;
   e.map = *map;
-  next = (next + 1) % kKvMapCache;
-  if (used < kKvMapCache) ++used;
+  next = (next + 1) % kMapCache;
+  if (used < kMapCache) ++used;
   return true;
+}
+
+// K or V: a (batch, heads, len, 128) strided view -> dims (d, len, heads, batch), box of
+// 64 dims x BN positions.
+bool make_kv_map(CUtensorMap* map, const void* base, const long long* st, long long batch, long long heads,
+                 long long len, int dtype) {
+  const long long dims[3] = {len, heads, batch}, strides[3] = {st[2], st[1], st[0]};
+  return make_map(map, base, dims, strides, BN, 1, dtype);
+}
+
+// Q: a (batch, q_heads, rows, 128) strided view -> dims (d, q_heads, rows, batch), box of
+// 64 dims x g heads x floor(128 / g) tree rows (one row tile of the pair kernel).
+bool make_q_map(CUtensorMap* map, const void* base, const long long* st, long long batch, long long q_heads,
+                long long rows, int group, int dtype) {
+  const long long dims[3] = {q_heads, rows, batch}, strides[3] = {st[1], st[2], st[0]};
+  return make_map(map, base, dims, strides, group, BM / group, dtype);
 }
 
 template <typename T, int MODE, typename MT>
@@ -1333,8 +1406,8 @@ int sm_count() {
 }
 
 template <typename T, bool SPLIT, bool TABLE>
-int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s, const KvRows& kvr,
-                cudaStream_t stream) {
+int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Sm100Args& s,
+                const KvRows& kvr, cudaStream_t stream) {
   auto kern = attn_pair_kernel<T, SPLIT, TABLE>;
   // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
   // per thread; any other count could leave the increase waiting for registers.
@@ -1352,10 +1425,11 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const Sm100Args& s
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
     if (dev >= 0) smem_set[dev] = true;
   }
-  const long long pairs = ((long long)s.group * s.rows + 2 * BM - 1) / (2 * BM);
+  const long long qrows = BM / s.group, mtiles = (s.rows + qrows - 1) / qrows;
+  const long long pairs = SPLIT ? 1 : (mtiles + 1) / 2;
   const long long items = (long long)s.batch * s.kv_heads * pairs;
   const long long grid = items < sm_count() ? items : sm_count();
-  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, s, kvr);
+  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, mq, s, kvr);
   return check_launch("speckv_tree_attention_bits(sm100)");
 }
 
@@ -1413,18 +1487,24 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   const KvRows kvr{a.row_table, (int)a.kv_batch};
   const bool bf = a.dtype == SPECKV_BF16;
   if (bits != nullptr) {
+    if (s.group > BM)
+      return fail(SPECKV_ENOSUPPORT, "speckv_tree_attention_bits: %d query heads per KV head (at most %d)", s.group,
+                  BM);
+    CUtensorMap mq;
+    if (!make_q_map(&mq, a.q, a.qs, a.batch, a.q_heads, a.rows, s.group, a.dtype))
+      return fail(SPECKV_ECUDA, "speckv_tree_attention_bits: cuTensorMapEncodeTiled failed for the query");
     // at most one 128-row tile per (sequence, KV head): the two warpgroups split the keys
     const bool split = (long long)s.group * s.rows <= BM, table = kvr.map != nullptr;
     if (bf) {
-      if (split) return table ? launch_pair<__nv_bfloat16, true, true>(mk, mv, s, kvr, stream)
-                              : launch_pair<__nv_bfloat16, true, false>(mk, mv, s, kvr, stream);
-      return table ? launch_pair<__nv_bfloat16, false, true>(mk, mv, s, kvr, stream)
-                   : launch_pair<__nv_bfloat16, false, false>(mk, mv, s, kvr, stream);
+      if (split) return table ? launch_pair<__nv_bfloat16, true, true>(mk, mv, mq, s, kvr, stream)
+                              : launch_pair<__nv_bfloat16, true, false>(mk, mv, mq, s, kvr, stream);
+      return table ? launch_pair<__nv_bfloat16, false, true>(mk, mv, mq, s, kvr, stream)
+                   : launch_pair<__nv_bfloat16, false, false>(mk, mv, mq, s, kvr, stream);
     }
-    if (split) return table ? launch_pair<__half, true, true>(mk, mv, s, kvr, stream)
-                            : launch_pair<__half, true, false>(mk, mv, s, kvr, stream);
-    return table ? launch_pair<__half, false, true>(mk, mv, s, kvr, stream)
-                 : launch_pair<__half, false, false>(mk, mv, s, kvr, stream);
+    if (split) return table ? launch_pair<__half, true, true>(mk, mv, mq, s, kvr, stream)
+                            : launch_pair<__half, true, false>(mk, mv, mq, s, kvr, stream);
+    return table ? launch_pair<__half, false, true>(mk, mv, mq, s, kvr, stream)
+                 : launch_pair<__half, false, false>(mk, mv, mq, s, kvr, stream);
   }
   const int min_group = a.mask_dtype == SPECKV_F32 ? mask_min_group<float>() : mask_min_group<uint16_t>();
   if (a.mask != nullptr && s.group >= min_group) {
