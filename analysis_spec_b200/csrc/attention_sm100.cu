@@ -188,6 +188,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// L2 prefetch of one box of a tensor map (no shared-memory destination, no barrier).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -668,7 +676,8 @@ __host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u;
 __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
 
 enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
-       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19, C_Q_EMPTY = 20, C_O_READ = 22 };
+       C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19, C_Q_EMPTY = 20, C_O_READ = 22,
+       C_PH_FULL = 24 };
 
 // Warp-wide forms: every lane runs the same code (the operands stay warp-uniform) and
 // one elected lane, always lane 0 with the full mask, issues the instruction; the
@@ -841,6 +850,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mbar_init(bar(C_Q_FULL + i), 1);
       mbar_init(bar(C_Q_EMPTY + i), 1);
       mbar_init(bar(C_P_FULL + i), 128);
+      mbar_init(bar(C_PH_FULL + i), 128);
     }
     mbar_init(bar(C_DRAIN), 1);
     mbar_init(bar(C_XCHG), 128);
@@ -880,6 +890,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // first key tile of sequence b, from the sort keys in shared memory when they exist
+  auto tile0_of = [&](int b) { return sorted ? n_tiles_all - keys[b] : first_tile(b); };
   const int G = gridDim.x, c = blockIdx.x;
   // slot k of this CTA -> global position (snake order over the sorted list)
   auto item_at = [&](int k, Item& it) -> bool {
@@ -922,19 +934,36 @@ __global__ void __launch_bounds__(kThreads2, 1)
           tma_load_4d(qd + kTileHalf, &tmq, bar(C_Q_FULL + t), 64, it.kvh * a.group, r0, it.b);
         }
         if (!ok) break;
-        const int t0 = first_tile(it.b);
-        int kb = it.b;  // K/V row of the sequence: through the row table when there is one
-        if (TABLE) {
-          const long long p = kvr.map[it.b];
+        const int t0 = tile0_of(it.b);
+        // K/V row of a sequence: through the row table when there is one
+        auto kv_row = [&](int b, bool report) {
+          if (!TABLE) return b;
+          const long long p = kvr.map[b];
           if (p < 0 || p >= kvr.rows) {
-            record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
-            kb = 0;
-          } else {
-            kb = (int)p;
+            if (report) record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
+            return 0;
           }
-        }
+          return (int)p;
+        };
+        const int kb = kv_row(it.b, true);
+        // three key tiles before this item ends, the next item's Q tiles and first K / V
+        // tiles are prefetched into L2, so that its start does not wait on DRAM
+        const int prefetch_at = max(t0, n_tiles_all - 3);
         for (int i = t0; i < n_tiles_all; ++i, ++cnt) {
           const int s = cnt & 1;
+          Item nx;
+          if (i == prefetch_at && item_at(k + 1, nx)) {
+            const int nq = (SPLIT || nx.pair * 2 + 1 >= mtiles) ? 1 : 2;
+            for (int t = 0; t < nq; ++t)
+              for (int h = 0; h < 2; ++h)
+                tma_prefetch_4d(&tmq, h * 64, nx.kvh * a.group, SPLIT ? 0 : (nx.pair * 2 + t) * qrows, nx.b);
+            const int nt0 = tile0_of(nx.b), nkb = kv_row(nx.b, false);
+            for (int j = nt0; j < nt0 + 2 && j < n_tiles_all; ++j)
+              for (int h = 0; h < 2; ++h) {
+                tma_prefetch_4d(&tmk, h * 64, j * BN, nx.kvh, nkb);
+                tma_prefetch_4d(&tmv, h * 64, j * BN, nx.kvh, nkb);
+              }
+          }
           if (cnt >= 2 && !mbar_wait(bar(C_K_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 21)) { ok = false; break; }
           const uint32_t kd = sbase + K2_OFF + s * kTileBytes;
           mbar_expect_tx(bar(C_K_FULL + s), kTileBytes);
@@ -994,16 +1023,29 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
         __syncwarp();
       };
+      // P.V in two halves: keys 0..63 as soon as the softmax has stored that half of P
+      // (C_PH_FULL), keys 64..127 after the rest (C_P_FULL). SPLIT publishes P at once and
+      // issues all eight MMAs after C_P_FULL (fewer live registers in its MMA warp).
       auto issue_pv = [&](int t, int stage, bool first) -> bool {
-        if (!wait(C_P_FULL + t, sc[t] & 1, 23)) return false;
-        ++sc[t];
-        tc_fence_after();
         const uint64_t bd = v_desc + (uint64_t)stage * kStageStep;
         const uint32_t d = tmem + O2_COL(t), pa = tmem + S_COL(t);
         const uint32_t acc0 = first ? 0u : 1u;
+        if (!SPLIT) {
+          if (!wait(C_PH_FULL + t, sc[t] & 1, 32)) return false;
+          tc_fence_after();
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < BN / 32; ++kk)
+              tc_mma_ts(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, kk > 0 ? 1u : acc0);
+          }
+          __syncwarp();
+        }
+        if (!wait(C_P_FULL + t, sc[t] & 1, 23)) return false;
+        ++sc[t];
+        tc_fence_after();
         if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
+          for (int kk = SPLIT ? 0 : BN / 32; kk < BN / 16; ++kk)
             tc_mma_ts(d, pa + kk * 8, bd + (uint64_t)(kk * (2048 >> 4)), id_pv, kk > 0 ? 1u : acc0);
         }
         __syncwarp();
@@ -1011,7 +1053,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
         if (SPLIT) {
-          const int n = n_tiles_all - first_tile(it.b);
+          const int n = n_tiles_all - tile0_of(it.b);
           ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
           tc_fence_after();
           // O0 and O1 of the previous item must be read (merged) before this item's first P.V
@@ -1056,7 +1098,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           continue;
         }
         const bool act1 = it.pair * 2 + 1 < mtiles;
-        const int n = n_tiles_all - first_tile(it.b);
+        const int n = n_tiles_all - tile0_of(it.b);
         ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
         if (ok && act1) ok = wait(C_Q_FULL + 1, ic[1] & 1, 25);
         tc_fence_after();
@@ -1135,7 +1177,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     bool have = next_item(k, it);
     const int i_first = SPLIT ? t : 0, i_step = SPLIT ? 2 : 1;  // this warpgroup's key tiles
     while (have) {
-      const int t0 = first_tile(it.b);
+      const int t0 = tile0_of(it.b);
       const int n = n_tiles_all - t0;
       const RowMap m = row_map(it);
       const uint32_t* brow = a.bits + ((long long)it.b * a.rows + m.r) * a.row_words + t0 * 4;
@@ -1172,7 +1214,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const float2 neg = make_float2(nm, nm);
         float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                           make_float2(0.f, 0.f)};  // independent partial sums: no 64-long add chain
-        // P = 2^(s * scale - m), packed to 16 bits over the first 64 columns of S;
+        // P = 2^(s * scale - m), packed to 16 bits over the first 64 columns of S, in two
+        // halves of 64 keys (the first half's P.V starts while the second is computed);
         // pairs on the MUFU ex2 unit or by polynomial on the FMA pipe (poly_pair)
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
@@ -1190,22 +1233,33 @@ __global__ void __launch_bounds__(kThreads2, 1)
             pk[j >> 1] = pack2<T>(e.x, e.y);
           }
           tmem_st8(s_addr + cc * 8, pk);
-        }
-        if (i > i_first && __any_sync(0xffffffffu, corr != 1.f)) {
-          // O_t holds tiles < i: their P.V MMAs were issued before S_t,i, and the commit
-          // that signalled S_t,i covers them; P_t,i . V_i waits for P_FULL below.
+          // O is rescaled before the first P.V of this tile: after the first half of P (only
+          // 64 scores still live) when the halves are published apart, else after all of P
+          if (cc == (SPLIT ? 7 : 3)) {
+            if (i > i_first && __any_sync(0xffffffffu, corr != 1.f)) {
+              // O_t holds tiles < i: their P.V MMAs were issued before S_t,i, and the commit
+              // that signalled S_t,i covers them; P_t,i . V_i waits for C_PH_FULL below.
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            float o[32];
-            tmem_ld32(o_addr + cc * 32, o);
-            tmem_wait_ld();
+              for (int oc = 0; oc < 4; ++oc) {
+                float o[32];
+                tmem_ld32(o_addr + oc * 32, o);
+                tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] *= corr;
-            tmem_st32(o_addr + cc * 32, o);
+                for (int j = 0; j < 32; ++j) o[j] *= corr;
+                tmem_st32(o_addr + oc * 32, o);
+              }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(C_PH_FULL + t));
           }
         }
-        tmem_wait_st();
-        tc_fence_before();
+        // (SPLIT: the draft-sized kernel publishes both halves at once, which keeps its
+        // register footprint)
+        if (!SPLIT) {
+          tmem_wait_st();
+          tc_fence_before();
+        }
         mbar_arrive(bar(C_P_FULL + t));
         const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
         l_run = l_run * corr + ((s01.x + s01.y) + (s23.x + s23.y));
