@@ -644,6 +644,22 @@ def history_pack(dst, pool, offsets, rows, max_length):
 
 
 @_on_device
+def acceptance_counts(packet, batch, proposed_per_row, counts):
+    """counts[:5] = the round's acceptance-counter increments from the packet rows (device)."""
+    _require_cuda(packet, counts)
+    if counts.dtype != torch.long or not counts.is_contiguous() or counts.numel() < 5:
+        raise ValueError('acceptance_counts: counts must be a contiguous int64 tensor of 5 entries')
+    if batch == 0:  # nothing to read (an empty packet may carry any strides)
+        _lib.call('speckv_acceptance_counts', None, 2, 0, int(proposed_per_row), counts.data_ptr(), _stream(counts))
+        return
+    if packet.dtype != torch.long or packet.dim() != 2 or packet.stride(1) != 1 or packet.shape[1] < 2 or \
+            packet.shape[0] < batch:
+        raise ValueError('acceptance_counts: packet must be a (batch, >= 2) int64 tensor with unit column stride')
+    _lib.call('speckv_acceptance_counts', packet.data_ptr(), packet.stride(0), int(batch), int(proposed_per_row),
+              counts.data_ptr(), _stream(packet))
+
+
+@_on_device
 def mask_bits(mask, bits, first_col, nonbinary):
     """Visibility bits of a dense additive (batch, 1, rows, columns) mask (any strides): bit set
     iff the entry is 0; lowest-value / -inf entries masked; any other value sets nonbinary[0]."""

@@ -10,8 +10,10 @@ accumulates after every verification (helper/opd_generate.py:551-555):
     verified_rows   += 1                    per row   (avg_acc_length[1])
     finished_rows   += eos flag of the row's packet
 
-The all_reduce of each round runs on a side stream, so it never sits between
-two KV kernels and never blocks the host. NCCL (CUDA tensors) and gloo (CPU
+On CUDA the increments come from the device packet (`add_device_round`, one
+small kernel), and the all_reduce of each round runs on a side stream: it never
+sits between two KV kernels, never blocks the host and never orders the next
+round's kernels after the other ranks. NCCL (CUDA tensors) and gloo (CPU
 tensors) both work; a rank that fails surfaces on the others as an error from
 their next `add_round`/`finish` once the process group's timeout expires.
 """
@@ -49,6 +51,11 @@ class AcceptanceCounters:
         self._cuda = self.device.type == 'cuda'
         self._stream = torch.cuda.Stream(self.device) if self._cuda else None
         self._total_dev = torch.zeros(len(FIELDS), dtype=torch.long, device=self.device) if self._cuda else None
+        # device rounds: a ring of per-round vectors, each reused once the side stream is done with it
+        self._ring = [torch.zeros(len(FIELDS), dtype=torch.long, device=self.device) for _ in range(3)] \
+            if self._cuda else None
+        self._ring_done = [None] * 3
+        self._rounds = 0
 
     def _collect(self):
         if self._work is not None:
@@ -76,6 +83,29 @@ class AcceptanceCounters:
             return
         self._work = dist.all_reduce(vec, group=self.group, async_op=True)
         self._vec = vec
+
+    def add_device_round(self, packet, batch, proposed_per_row):
+        """Queues the reduction of this round's increments, computed on the device from the
+        schedule packet (rows [length, eos?, ...]) by one kernel on the current stream; the
+        all_reduce and the accumulation run on the side stream. Nothing here waits for the
+        other ranks: a ring slot is reused three rounds later, by when its reduction is done."""
+        import torch.distributed as dist
+        from . import _ops
+        slot = self._rounds % len(self._ring)
+        self._rounds += 1
+        vec = self._ring[slot]
+        cur = torch.cuda.current_stream(self.device)
+        if self._ring_done[slot] is not None:
+            cur.wait_event(self._ring_done[slot])
+        _ops.acceptance_counts(packet, batch, proposed_per_row, vec)
+        self._stream.wait_stream(cur)
+        with torch.cuda.stream(self._stream):
+            if self.distributed:
+                dist.all_reduce(vec, group=self.group, async_op=True).wait()  # the side stream waits
+            self._total_dev.add_(vec)
+            done = torch.cuda.Event()
+            done.record(self._stream)
+        self._ring_done[slot] = done
 
     def fence(self, stream=None):
         """Orders `stream` (default: the current one) after the reductions queued so far. Call it

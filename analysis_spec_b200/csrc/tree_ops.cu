@@ -386,10 +386,63 @@ __global__ void position_update_kernel(PositionArgs a, long long batch, long lon
   position_row(a, b, past, width, threadIdx.x & 31, err);
 }
 
+// ---------------------------------------------------------------------------
+// acceptance counters of a round from the packet rows [length, eos?, ...]: one CTA,
+// a thread per row (strided), block reduction; writes (does not accumulate) the five sums.
+// ---------------------------------------------------------------------------
+constexpr int kCountThreads = 256;
+__global__ void __launch_bounds__(kCountThreads) acceptance_counts_kernel(const int64_t* __restrict__ packet,
+                                                                          long long stride, long long batch,
+                                                                          long long proposed, int64_t* counts) {
+  __shared__ long long part[kCountThreads / 32][3];
+  long long accepted = 0, length = 0, finished = 0;
+  for (long long b = threadIdx.x; b < batch; b += kCountThreads) {
+    const long long len = packet[b * stride], eos = packet[b * stride + 1];
+    accepted += len > 1 ? len - 1 : 0;
+    length += len;
+    finished += eos != 0;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    accepted += __shfl_xor_sync(0xffffffffu, accepted, o);
+    length += __shfl_xor_sync(0xffffffffu, length, o);
+    finished += __shfl_xor_sync(0xffffffffu, finished, o);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    part[warp][0] = accepted;
+    part[warp][1] = length;
+    part[warp][2] = finished;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long sums[3] = {0, 0, 0};
+    for (int w = 0; w < kCountThreads / 32; ++w)
+      for (int k = 0; k < 3; ++k) sums[k] += part[w][k];
+    counts[0] = sums[0];
+    counts[1] = proposed * batch;
+    counts[2] = sums[1];
+    counts[3] = batch;
+    counts[4] = sums[2];
+  }
+}
+
 }  // namespace
 }  // namespace speckv
 
 using namespace speckv;
+
+extern "C" int speckv_acceptance_counts(const int64_t* packet, int64_t packet_stride_b, int64_t batch,
+                                        int64_t proposed_per_row, int64_t* counts, void* stream) {
+  const char* fn = "speckv_acceptance_counts";
+  if (batch < 0 || proposed_per_row < 0) return fail(SPECKV_EINVAL, "%s: negative size", fn);
+  if (batch > 0 && packet_stride_b < 2) return fail(SPECKV_EINVAL, "%s: packet rows need 2 columns", fn);
+  if (counts == nullptr || (batch > 0 && packet == nullptr)) return fail(SPECKV_EINVAL, "%s: null pointer", fn);
+  const int st = check_current_device(fn, {packet, counts});
+  if (st) return st;
+  acceptance_counts_kernel<<<1, kCountThreads, 0, static_cast<cudaStream_t>(stream)>>>(packet, packet_stride_b,
+                                                                                     batch, proposed_per_row, counts);
+  return check_launch(fn);
+}
 
 extern "C" int speckv_trace_path(const int64_t* parents, const int64_t* tokens, const int64_t* contexts,
                                  const int64_t* samples, int64_t batch, int64_t rows, int64_t eos,

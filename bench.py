@@ -20,7 +20,9 @@ Reported (one JSON line on rank 0):
   e2e        the same KV-commit metric through the public API with the step's
              inputs copied from pinned host memory and the packet read back
   roofline   the append kernel (dominant commit kernel) vs measured HBM copy peak
-  cpu_baseline  the CPU oracle on a bounded sample of the same work
+  cpu_baseline  the reference's torch CPU branch of the commit, restated on host tensors
+             (oracle/torch_commit.py, pinned to the reference's own code), all layers, host cores;
+             cpu_baseline_c_port: the C/OpenMP restatement on a sample of the layers
   draft_step   one draft expansion step (mask + attention of one draft layer),
              this library's launches beside the reference's torch sequence
   history_step the accepted-feature gather + rollout-history append of a round,
@@ -28,8 +30,9 @@ Reported (one JSON line on rank 0):
   release_step releasing a quarter of the sequences: the reference's swap_remove
              (history moves) against a row-table cache (table rewrite, no KV bytes)
 
-``--impl reference`` times the CPU restatement of the reference's path (the
-reference is Python/torch and cannot run on the GPU host) on the host cores.
+``--impl reference`` times the reference's torch CPU branch of the commit, restated
+(the reference is Python/torch and is not present on the GPU host; the restatement is
+pinned to it by oracle/pin_torch_commit.py), on the host cores.
 Multi-GPU (torchrun): every rank owns its own batch of sequences (weak scaling)
 and one int64 acceptance-counter all_reduce runs per step on a side stream.
 """
@@ -299,8 +302,6 @@ def verify_round(st, i, marks=None):
     vis = st.tree.visibility(st.past, st.pad, workspace=st.vis_ws)
     mark(1)
     views = append()
-    if getattr(st, 'counters', None) is not None:
-        st.counters.fence()  # the previous round's counter all_reduce leaves the SMs first
     mark(2)
     if getattr(st, 'attn_graph', None) is not None:
         st.attn_graph.replay()  # the same 36 launches, captured once (capture_attention)
@@ -382,8 +383,13 @@ def run_ours(args):
     counters = AcceptanceCounters(device)
     st.counters = counters
 
+    host_totals = [0] * 5  # the same increments summed from the host packet rows, as a check
+
     def reduce_counters(rows):
-        counters.add_round(round_increments(rows, wl.nodes))
+        # increments computed on the device from the packet; the all_reduce runs on a side stream
+        counters.add_device_round(st.packet, wl.batch, wl.nodes)
+        for k, v in enumerate(round_increments(rows, wl.nodes)):
+            host_totals[k] += v
 
     for i in range(args.warmup):
         _, _, rows = verify_round(st, i)
@@ -416,6 +422,11 @@ def run_ours(args):
     launches = _lib.profile.calls + (args.steps * wl.layers if not args.no_graph else 0)
     kernel_ms = {name: [s.elapsed_time(e) for s, e in pairs] for name, pairs in _lib.profile.events.items()}
     totals = counters.finish()
+    if world > 1:  # the device totals are job-wide: sum the host check over the ranks too
+        check = torch.tensor(host_totals, dtype=torch.long, device=device)
+        dist.all_reduce(check)
+        host_totals = check.tolist()
+    totals['matches_host_packet_rows'] = list(totals.values()) == host_totals
     if world > 1:
         dist.barrier()
     clock = clocks.stop() if clocks else None
@@ -453,10 +464,10 @@ def run_ours(args):
         'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
-        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}',
-                                       'commit_bytes_per_step': commit_bytes // args.steps}),
+        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}'}),
         'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4), 'peak_gbs': hbm,
                       'ms_per_step': round(commit_ms / args.steps, 4),
+                      'bytes_per_step_per_gpu': commit_bytes // args.steps,
                       'launches': ['speckv_append_rows', 'speckv_commit_round'],
                       'append_region_ms_per_step': round(region_ms / args.steps, 4)},
         'tree_verify': {'steps_per_s': round(world * args.steps / (verify_ms * 1e-3), 3),
@@ -472,6 +483,7 @@ def run_ours(args):
                      'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
         'gpu_launches': launches,
+        'attention_launches': attention_launches(),
         'acceptance': totals,
         'clocks': clock,
         'e2e': e2e,
@@ -480,11 +492,22 @@ def run_ours(args):
         'release_step': release,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result['cpu_baseline'] = cpu_baseline(wl, budget_s=12.0)
+        result['cpu_baseline'] = cpu_baseline(wl, budget_s=10.0)
+        result['cpu_baseline_c_port'] = c_port_baseline(wl, budget_s=6.0)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def attention_launches():
+    """Attention launches the library issued in this process, per kernel family (calls only:
+    graph replays are not counted); cuda_core > 0 would mean a shape left the tensor cores."""
+    import ctypes
+    from analysis_spec_b200 import _lib
+    tc, cc = ctypes.c_int64(0), ctypes.c_int64(0)
+    _lib.call('speckv_attention_launches', ctypes.byref(tc), ctypes.byref(cc))
+    return {'tensor_core': tc.value, 'cuda_core': cc.value}
 
 
 def time_steps(fn, iters, warmup, spin_ms=8.0):
@@ -800,7 +823,8 @@ class CpuCommit:
         return self.append_bytes + self.layers * 2 * 2 * wl.batch * wl.kv_heads * (width - ext) * self.row_bytes
 
 
-def cpu_baseline(wl, budget_s=12.0, layers=4):
+def c_port_baseline(wl, budget_s=6.0, layers=4):
+    """The C/OpenMP restatement of the commit (a much faster CPU code than the reference's)."""
     cpu = CpuCommit(wl, layers)
     cpu.step(0)
     moved, steps, t0 = 0, 0, time.perf_counter()
@@ -809,33 +833,71 @@ def cpu_baseline(wl, budget_s=12.0, layers=4):
         steps += 1
     dt = time.perf_counter() - t0
     return {'value': round(moved / dt / 1e9, 4), 'unit': 'GB/s', 'cores': cpu.oracle.max_threads(), 'kind': 'port',
-            'sample': f'{layers} of {wl.layers} layers per step (full batch {wl.batch}, 61 tree rows), '
-                      f'{steps} steps in {dt:.1f} s: append + trace + schedule + compaction by the C/numpy oracle'}
+            'sample': f'{layers} of {wl.layers} layers per step (full batch {wl.batch}, {wl.rows} tree rows), '
+                      f'{steps} steps in {dt:.1f} s: append + trace + schedule + compaction by the C/OpenMP oracle'}
+
+
+def torch_commit(wl, seed=7):
+    """The reference's torch CPU branch of the commit, restated on host tensors, all layers."""
+    import torch
+    from analysis_spec_b200 import workloads as W
+    from oracle.torch_commit import TorchCommit
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.RandomState(seed)
+    past = int(W.prefix_lengths(rng, wl.prefix, wl.batch).max())
+    parents, tokens = W.packed_trees(rng, wl.batch, wl.nodes, wl.depth, wl.topk)
+    samples = [W.samples_for(rng, parents, tokens, W.accepted_lengths(rng, wl.accept, wl.batch)) for _ in range(4)]
+    return TorchCommit(wl.layers, wl.batch, wl.kv_heads, wl.dim, wl.rows, past, parents, tokens, samples, wl.depth,
+                       dtype=getattr(torch, wl.dtype))
+
+
+def torch_commit_sample(wl, rounds):
+    pin = ROOT / 'oracle' / 'torch_commit_pin.json'
+    pinned = ''
+    if pin.exists():
+        p = json.loads(pin.read_text())
+        pinned = (f"; pinned against the reference's own code on {p['threads']} threads of {p['cpu']}: "
+                  f"caches identical, {p['reference_s_per_round']} s per round for the reference vs "
+                  f"{p['restatement_s_per_round']} s for the restatement")
+    return (f'{rounds} verify rounds of all {wl.layers} layers (batch {wl.batch}, {wl.rows} tree rows, {wl.dtype}): '
+            'the reference torch CPU branch restated (per layer two copy_ appends, torch.gather of the accepted '
+            'rows into a reused scratch and a copy back; trace + schedule; position update)' + pinned)
+
+
+def cpu_baseline(wl, budget_s=10.0):
+    import torch
+    tc = torch_commit(wl)
+    tc.round(0, EOS)
+    moved, rounds, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        moved += tc.round(rounds, EOS)
+        rounds += 1
+    dt = time.perf_counter() - t0
+    return {'value': round(moved / dt / 1e9, 4), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'kind': 'port',
+            'sample': torch_commit_sample(wl, rounds) + f', {dt:.1f} s'}
 
 
 def run_reference(args):
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
+    import torch
     wl = workload(args)
-    cpu = CpuCommit(wl, layers=min(4, wl.layers))
+    tc = torch_commit(wl)
     for i in range(args.warmup):
-        cpu.step(i)
+        tc.round(i, EOS)
     moved, t0 = 0, time.perf_counter()
     for i in range(args.steps):
-        moved += cpu.step(i)
+        moved += tc.round(i, EOS)
     dt = time.perf_counter() - t0
     value = moved / dt / 1e9
-    sample = (f'each step: 4 of {wl.layers} layers of the workload (full batch {wl.batch}); append + trace + '
-              'schedule + compaction by the C/numpy restatement of the reference (the reference itself is '
-              'Python/torch code that is not present on the GPU host)')
     print(json.dumps({
         'impl': 'reference', 'metric': METRIC, 'value': round(value, 4), 'unit': 'GB/s', 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(dt * 1e3 / args.steps, 3),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
-        'config': workload_config(wl, {'parallelism': 'host cores'}),
-        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': cpu.oracle.max_threads(), 'kind': 'port',
-                         'sample': sample},
+        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{args.gpus}'}),
+        'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'kind': 'port',
+                         'sample': torch_commit_sample(wl, args.steps)},
         'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
 

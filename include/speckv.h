@@ -370,6 +370,19 @@ int speckv_position_update(uint8_t* pad_rows, int64_t pad_rows_stride, int64_t p
                            int64_t past, int64_t width, int64_t* positions,
                            int64_t positions_stride_b, int64_t* past_positions, void* stream);
 
+/* Acceptance counters of one verify round, from the schedule packet's rows
+ * [length, last token == eos, ...] (row stride packet_stride_b int64):
+ *   counts[0] = sum over rows of max(length - 1, 0)   (accepted draft tokens)
+ *   counts[1] = proposed_per_row * batch              (proposed draft tokens)
+ *   counts[2] = sum of lengths, counts[3] = batch      (accepted-length sum / rows)
+ *   counts[4] = rows whose last token is eos
+ * (written, not accumulated; counts is a device array of 5 int64). The
+ * increments helper/opd_generate.py:551-555 adds on the host after each
+ * verification, computed on the device so that a sequence-sharded job can
+ * all_reduce them without a host round trip. */
+int speckv_acceptance_counts(const int64_t* packet, int64_t packet_stride_b, int64_t batch,
+                             int64_t proposed_per_row, int64_t* counts, void* stream);
+
 /* ---- tree-verify attention -------------------------------------------- */
 
 /* GQA attention of `rows` tree queries over kv_len cached positions with an
