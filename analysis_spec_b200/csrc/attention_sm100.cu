@@ -641,12 +641,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // projection; rows q * g .. 127 stay zero (they are never written).
 //
 //   warp 0      TMA producer: the Q tiles of the next item (as soon as the last
-//               S MMA of the current item has read the Q buffer), then K and V
-//               tiles in separate 2-stage rings
+//               S MMA of the current item has read the Q buffer), then the K tiles
+//               of a 2-stage ring
+//   warp 2      TMA producer of the V tiles (2-stage ring)
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
 //               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
 //               warpgroup works while the tensor pipe serves the other tile
-//   warps 2-3   idle (they complete the first warpgroup for the register split)
+//   warp 3      idle (it completes the first warpgroup for the register split)
 //   warps 4-7   softmax of row tile 0; warps 8-11 softmax of row tile 1: thread =
 //               row = TMEM lane (warp % 4 picks the lane quarter); S is read once
 //               into registers, P (16-bit) goes back into the first 64 columns of
@@ -906,22 +907,38 @@ __global__ void __launch_bounds__(kThreads2, 1)
 
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers ----------------
+    // One thread issues TMA loads at about 50 GB/s, below what the K / V rings need, so
+    // two warps share the work: warp 0 loads the Q tiles and the K ring (and prefetches
+    // the next item into L2), warp 2 the V ring. Both walk the same item list.
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
-      int cnt = 0, issued_k = 0, issued_v = 0;
-      int qc[2] = {0, 0};           // Q tiles requested per row tile
+      const bool kq = warp == 0;
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(kq ? &tmk : &tmv)) : "memory");
+      if (kq) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
+      const CUtensorMap* map = kq ? &tmk : &tmv;
+      const int full0 = kq ? C_K_FULL : C_V_FULL, empty0 = kq ? C_K_EMPTY : C_V_EMPTY;
+      const uint32_t ring = sbase + (kq ? K2_OFF : V2_OFF);
+      int cnt = 0, issued = 0;
+      int qc[2] = {0, 0};                 // Q tiles requested per row tile
       bool q_issued[2] = {false, false};  // the latest request was sent (not withheld)
-      const bool withhold = blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0;
+      const bool withhold = kq && blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0;
       const uint32_t q_bytes = 2u * 128u * (uint32_t)(qrows * a.group);  // two 64-dim halves of q * g rows
       bool ok = true;
       Item it;
+      // K/V row of a sequence: through the row table when there is one
+      auto kv_row = [&](int b, bool report) {
+        if (!TABLE) return b;
+        const long long p = kvr.map[b];
+        if (p < 0 || p >= kvr.rows) {
+          if (report) record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
+          return 0;
+        }
+        return (int)p;
+      };
       for (int k = 0; ok && item_at(k, it); ++k) {
         // Q tiles of the item: each buffer is free once the previous item's last S MMA has read it
-        const int ntq = (SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2;
+        const int ntq = !kq ? 0 : ((SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2);
         for (int t = 0; t < ntq; ++t) {
           if (qc[t] >= 1 && !mbar_wait(bar(C_Q_EMPTY + t), (qc[t] - 1) & 1, abort_flag, a.err, 20)) { ok = false; break; }
           ++qc[t];
@@ -935,24 +952,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
         }
         if (!ok) break;
         const int t0 = tile0_of(it.b);
-        // K/V row of a sequence: through the row table when there is one
-        auto kv_row = [&](int b, bool report) {
-          if (!TABLE) return b;
-          const long long p = kvr.map[b];
-          if (p < 0 || p >= kvr.rows) {
-            if (report) record_error(a.err, SPECKV_DERR_ROW_TABLE, p);
-            return 0;
-          }
-          return (int)p;
-        };
-        const int kb = kv_row(it.b, true);
+        const int kb = kv_row(it.b, kq);
         // three key tiles before this item ends, the next item's Q tiles and first K / V
         // tiles are prefetched into L2, so that its start does not wait on DRAM
         const int prefetch_at = max(t0, n_tiles_all - 3);
         for (int i = t0; i < n_tiles_all; ++i, ++cnt) {
           const int s = cnt & 1;
           Item nx;
-          if (i == prefetch_at && item_at(k + 1, nx)) {
+          if (kq && i == prefetch_at && item_at(k + 1, nx)) {
             const int nq = (SPLIT || nx.pair * 2 + 1 >= mtiles) ? 1 : 2;
             for (int t = 0; t < nq; ++t)
               for (int h = 0; h < 2; ++h)
@@ -964,25 +971,21 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 tma_prefetch_4d(&tmv, h * 64, j * BN, nx.kvh, nkb);
               }
           }
-          if (cnt >= 2 && !mbar_wait(bar(C_K_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 21)) { ok = false; break; }
-          const uint32_t kd = sbase + K2_OFF + s * kTileBytes;
-          mbar_expect_tx(bar(C_K_FULL + s), kTileBytes);
-          tma_load_4d(kd, &tmk, bar(C_K_FULL + s), 0, i * BN, it.kvh, kb);
-          tma_load_4d(kd + kTileHalf, &tmk, bar(C_K_FULL + s), 64, i * BN, it.kvh, kb);
-          issued_k = cnt + 1;
-          if (cnt >= 2 && !mbar_wait(bar(C_V_EMPTY + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, 22)) { ok = false; break; }
-          const uint32_t vd = sbase + V2_OFF + s * kTileBytes;
-          mbar_expect_tx(bar(C_V_FULL + s), kTileBytes);
-          tma_load_4d(vd, &tmv, bar(C_V_FULL + s), 0, i * BN, it.kvh, kb);
-          tma_load_4d(vd + kTileHalf, &tmv, bar(C_V_FULL + s), 64, i * BN, it.kvh, kb);
-          issued_v = cnt + 1;
+          if (cnt >= 2 && !mbar_wait(bar(empty0 + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, kq ? 21 : 22)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = ring + s * kTileBytes;
+          mbar_expect_tx(bar(full0 + s), kTileBytes);
+          tma_load_4d(dst, map, bar(full0 + s), 0, i * BN, it.kvh, kb);
+          tma_load_4d(dst + kTileHalf, map, bar(full0 + s), 64, i * BN, it.kvh, kb);
+          issued = cnt + 1;
         }
       }
       // Loads still in flight must land before shared memory is released: after an abort
       // (which may come after this loop ended) nobody consumes them; in a normal run
       // these phases completed long ago and the waits return at once.
-      for (int q = issued_k - 2 < 0 ? 0 : issued_k - 2; q < issued_k; ++q) drain_wait(bar(C_K_FULL + (q & 1)), (q >> 1) & 1);
-      for (int q = issued_v - 2 < 0 ? 0 : issued_v - 2; q < issued_v; ++q) drain_wait(bar(C_V_FULL + (q & 1)), (q >> 1) & 1);
+      for (int q = issued - 2 < 0 ? 0 : issued - 2; q < issued; ++q) drain_wait(bar(full0 + (q & 1)), (q >> 1) & 1);
       for (int t = 0; t < 2; ++t)
         if (qc[t] >= 1 && q_issued[t]) drain_wait(bar(C_Q_FULL + t), (qc[t] - 1) & 1);
     }

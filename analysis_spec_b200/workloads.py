@@ -7,10 +7,11 @@ Shapes follow the benchmark configurations of the path:
                      prefix U{256..2048}, 60-node tree (depth 6, top-k 10),
                      accepted length ~ geometric(mean 3.5) capped at 7
   qwen25_3b_attn     as qwen25_3b with prefix U{256..3072} and Q/K/V ~ 0.5 N(0, 1)
-  qwen25_7b          28 layers, 28 q / 4 KV heads, batch 256 (sharded by sequence), max_len 8192,
-                     prefix U{512..6144}
-  qwen25_14b         48 layers, 40 q / 8 KV heads, batch 128, max_len 16384,
-                     prefix log-uniform [128, 14000], 25% of sequences finish per step
+  qwen25_7b          28 layers, 28 q / 4 KV heads, batch 256 split over the GPUs of the job
+                     (strong scaling), max_len 8192, prefix U{512..6144}
+  qwen25_14b         48 layers, 40 q / 8 KV heads, batch 16 per GPU (128 over 8 GPUs), max_len
+                     16384, prefix log-uniform [128, 14000], 25% of sequences finish per step and
+                     as many new ones are admitted
 Sequences share one physical cache length (the longest prefix); shorter
 prefixes are left-padded and their padding columns hidden by the padding
 bitmap, as the reference's prefill lays them out.
@@ -52,8 +53,8 @@ WORKLOADS = {
     'qwen25_3b_attn': Workload('qwen25_3b_attn', 36, 64, 16, 2, 128, 'bfloat16', 4096, ('uniform', 256, 3072), 60, 6,
                                10, ('geometric', 3.5, 7), qkv_scale=0.5),
     'qwen25_7b': Workload('qwen25_7b', 28, 256, 28, 4, 128, 'bfloat16', 8192, ('uniform', 512, 6144), 60, 6, 10,
-                          ('geometric', 3.5, 7)),
-    'qwen25_14b': Workload('qwen25_14b', 48, 128, 40, 8, 128, 'bfloat16', 16384, ('loguniform', 128, 14000), 60, 6,
+                          ('geometric', 3.5, 7), extra={'split_batch': True}),
+    'qwen25_14b': Workload('qwen25_14b', 48, 16, 40, 8, 128, 'bfloat16', 16384, ('loguniform', 128, 14000), 60, 6,
                            10, ('geometric', 3.5, 7), finish_fraction=0.25),
 }
 

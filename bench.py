@@ -71,6 +71,8 @@ def parse():
                    help="launch the round's attention layer by layer instead of replaying its CUDA graph")
     p.add_argument('--side-only', action='store_true',
                    help='only the draft-step and history-step measurements, on a one-layer cache (profiling)')
+    p.add_argument('--row-table', action='store_true',
+                   help='rollout workloads: release and admit through a row table instead of moving histories')
     return p.parse_args()
 
 
@@ -78,6 +80,9 @@ def workload(args):
     from dataclasses import replace
     from analysis_spec_b200.workloads import WORKLOADS
     wl = WORKLOADS[args.workload]
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    if wl.extra.get('split_batch') and world > 1:  # a job-wide batch sharded over the GPUs (strong scaling)
+        wl = replace(wl, batch=wl.batch // world)
     if args.layers:
         wl = replace(wl, layers=args.layers)
     if args.batch:
@@ -215,7 +220,7 @@ class Clocks:
 class Round:
     """Device-resident inputs of the stationary verify round (shapes never change)."""
 
-    def __init__(self, wl, device, seed, sample_sets=8):
+    def __init__(self, wl, device, seed, sample_sets=8, row_table=False):
         import torch
         from analysis_spec_b200 import workloads as W
         from analysis_spec_b200.opd_static_cache import OPDStaticCache
@@ -235,7 +240,7 @@ class Round:
         self.pad_commit = torch.zeros_like(self.pad)
         gen = torch.Generator(device=device).manual_seed(seed)
         scale = wl.qkv_scale
-        self.cache = OPDStaticCache(wl.capacity, batch_capacity=B)
+        self.cache = OPDStaticCache(wl.capacity, batch_capacity=B, row_table=row_table)
         prefix_k = (scale * torch.randn(B, H, self.past, D, device=device, generator=gen)).to(dtype)
         prefix_v = (scale * torch.randn(B, H, self.past, D, device=device, generator=gen)).to(dtype)
         for l in range(wl.layers):
@@ -307,8 +312,9 @@ def verify_round(st, i, marks=None):
         st.attn_graph.replay()  # the same 36 launches, captured once (capture_attention)
     else:
         for l in range(st.wl.layers):
-            _ops.tree_attention_bits(st.queries[l], views[l][0], views[l][1], vis.bits, vis.first_col, st.scale,
-                                     out=st.out[l])
+            k, v = views[l]
+            _ops.tree_attention_bits(st.queries[l], k, v, vis.bits, vis.first_col, st.scale, out=st.out[l],
+                                     row_table=getattr(k, '_speckv_rows', None))  # row-table caches only
     mark(3)
     path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
     rows, _, _, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
@@ -463,8 +469,10 @@ def run_ours(args):
     result = {
         'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
-        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
-        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}'}),
+        'scaling': 'strong' if wl.extra.get('split_batch') else 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+        'data': 'synthetic (seeded)',
+        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}',
+                                       'global_batch': wl.batch * world}),
         'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4), 'peak_gbs': hbm,
                       'ms_per_step': round(commit_ms / args.steps, 4),
                       'bytes_per_step_per_gpu': commit_bytes // args.steps,
@@ -895,11 +903,145 @@ def run_reference(args):
         'impl': 'reference', 'metric': METRIC, 'value': round(value, 4), 'unit': 'GB/s', 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(dt * 1e3 / args.steps, 3),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
-        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{args.gpus}'}),
+        'config': workload_config(wl, {'parallelism': f'sequence-sharded x{args.gpus}',
+                                       'global_batch': wl.batch * args.gpus}),
         'cpu_baseline': {'value': round(value, 4), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'kind': 'port',
                          'sample': torch_commit_sample(wl, args.steps)},
         'e2e': {'value': round(value, 4), 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
+
+
+def run_rollout(args):
+    """Rollout workloads (a fraction of the sequences finishes every step): each timed step is
+    a verify round (append, attention of every layer, trace, schedule, device commit, crop)
+    followed by the release of the finished sequences (the reference's swap_remove: the
+    surviving tail sequences' histories move into the holes; with --row-table a table rewrite)
+    and the admission of as many new sequences with fresh prefixes (one append launch for all
+    layers into the freed rows). KV-commit GB/s counts append + compaction + release +
+    admission bytes (each moved byte read once and written once; admission counts the new
+    prefixes' own positions) over the device time of those launches."""
+    import torch
+    import torch.distributed as dist
+    from analysis_spec_b200 import _lib, _ops
+    from analysis_spec_b200 import workloads as W
+    from analysis_spec_b200.build import build
+    from analysis_spec_b200.counters import AcceptanceCounters
+    from analysis_spec_b200.opd_static_cache import swap_remove_plan
+
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    if rank == 0:
+        build()
+    torch.cuda.set_device(local)
+    device = torch.device('cuda', local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
+    _lib.load()
+    wl = workload(args)
+    st = Round(wl, device, seed=1000 + rank, row_table=args.row_table)
+    counters = AcceptanceCounters(device)
+    B, H, D, L = wl.batch, wl.kv_heads, wl.dim, wl.layers
+    k_new = max(1, int(round(B * wl.finish_fraction)))
+    es = st.dtype.itemsize if hasattr(st.dtype, 'itemsize') else 2
+    rng = np.random.RandomState(4242 + rank)
+    # fresh prefixes of the admitted sequences, left-padded to the shared length (one source for all layers)
+    gen = torch.Generator(device=device).manual_seed(77 + rank)
+    fresh_k = (wl.qkv_scale * torch.randn(k_new, H, st.past, D, device=device, generator=gen)).to(st.dtype)
+    fresh_v = (wl.qkv_scale * torch.randn(k_new, H, st.past, D, device=device, generator=gen)).to(st.dtype)
+    cols = st.pad.shape[1]
+
+    def step(i, ev):
+        w, e, rows = verify_round(st, i)
+        counters.add_device_round(st.packet, B, wl.nodes)
+        commit = st.append_bytes + st.compact_bytes(w, e)
+        finished = [False] * B
+        for j in rng.choice(B, size=k_new, replace=False):
+            finished[j] = True
+        keep, sources, holes = swap_remove_plan(finished)
+        length = st.cache.layers[0].length
+        ev[0].record()
+        st.cache.swap_remove(len(keep), torch.tensor(sources, dtype=torch.long, device=device),
+                             torch.tensor(holes, dtype=torch.long, device=device))
+        ev[1].record()
+        release = 0 if args.row_table else len(sources) * L * 2 * 2 * H * length * D * es
+        new_len = W.prefix_lengths(rng, wl.prefix, k_new)
+        st.cache.admit([fresh_k] * L, [fresh_v] * L)
+        ev[2].record()
+        admit = int(new_len.sum()) * L * 2 * 2 * H * D * es
+        # the admitted rows' padding: left padding up to their own prefix, nothing in the tree columns
+        pad_new = np.zeros((k_new, cols), dtype=bool)
+        pad_new[:, :st.past] = W.left_padding(new_len, st.past)
+        st.pad[len(keep):].copy_(torch.from_numpy(pad_new), non_blocking=True)
+        return commit, release, admit
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        step(i, evs[i])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = Clocks(f'GPU-{torch.cuda.get_device_properties(device).uuid}') if rank == 0 else None
+    if clocks:
+        clocks.start()
+    _lib.profile.reset()
+    _lib.profile.enabled = True
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    moved = np.zeros(3)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(args.steps):
+        moved += step(args.warmup + i, evs[args.warmup + i])
+    end.record()
+    torch.cuda.synchronize()
+    _lib.profile.enabled = False
+    totals = counters.finish()
+    clock = clocks.stop() if clocks else None
+    kernel_ms = {name: [a.elapsed_time(b) for a, b in pairs] for name, pairs in _lib.profile.events.items()}
+    timed = evs[args.warmup:]
+    release_ms = sum(e[0].elapsed_time(e[1]) for e in timed)
+    admit_ms = sum(e[1].elapsed_time(e[2]) for e in timed)
+    commit_calls = kernel_ms.get('speckv_commit_round', [])
+    append_calls = kernel_ms.get('speckv_append_rows', [])
+    # append_rows serves both the round's append (deferred plan) and the admission (one call per step)
+    round_append_ms = sum(append_calls) - (admit_ms if not args.row_table else 0)
+    commit_ms = sum(commit_calls) + max(round_append_ms, 0.0) + release_ms + admit_ms
+    attn_ms = sum(kernel_ms.get('speckv_tree_attention_bits', []))
+    total_ms = start.elapsed_time(end)
+    times = torch.tensor([total_ms, commit_ms, attn_ms], device=device, dtype=torch.float64)
+    job = torch.tensor(moved, device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.all_reduce(job)
+        dist.barrier()
+        dist.destroy_process_group()
+    total_ms, commit_ms, attn_ms = times.tolist()
+    commit_b, release_b, admit_b = job.tolist()
+    value = (commit_b + release_b + admit_b) / (commit_ms * 1e-3) / 1e9
+    hbm, tflops, peak_kind = peaks()
+    attn_tflops = st.attention_flops() / (attn_ms / args.steps * 1e-3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic (seeded)',
+            'config': workload_config(wl, {'parallelism': f'sequence-sharded x{world}',
+                                           'release': 'row table' if args.row_table else 'swap_remove (moves)',
+                                           'finish_per_step': k_new}),
+            'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4),
+                          'bytes_per_step_job': {'append_compact': commit_b / args.steps,
+                                                 'release': release_b / args.steps, 'admit': admit_b / args.steps},
+                          'ms_per_step': round(commit_ms / args.steps, 4),
+                          'release_ms_per_step': round(release_ms / args.steps, 4),
+                          'admit_ms_per_step': round(admit_ms / args.steps, 4)},
+            'tree_verify': {'steps_per_s': round(args.steps / (attn_ms * 1e-3), 3),
+                            'attention_tflops': round(attn_tflops, 2),
+                            'roofline': {'bound': 'tensor', 'achieved': round(attn_tflops, 2), 'peak': tflops,
+                                         'unit': 'TFLOP/s', 'frac': round(attn_tflops / tflops, 4),
+                                         'peak_kind': peak_kind}},
+            'attention_launches': attention_launches(), 'acceptance': totals, 'clocks': clock,
+            'gpu_launches': _lib.profile.calls}), flush=True)
 
 
 if __name__ == '__main__':
@@ -909,4 +1051,8 @@ if __name__ == '__main__':
     elif a.side_only:
         run_side(a)
     else:
-        run_ours(a)
+        from analysis_spec_b200.workloads import WORKLOADS
+        if WORKLOADS[a.workload].finish_fraction > 0:
+            run_rollout(a)
+        else:
+            run_ours(a)
