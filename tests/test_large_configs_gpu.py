@@ -1,0 +1,129 @@
+"""Parity at the long-context configurations: Qwen2.5-7B (28 q / 4 KV heads, prefixes to 6144)
+and Qwen2.5-14B (40 q / 8 KV heads, 48 layers, prefixes log-uniform to 14000 in a 16384 cache).
+
+Attention is checked on slices of sequences against the float32 oracle (max |err| <= 2e-2,
+mean <= 2e-3, the criteria the path states); the KV commit at 48 layers x 8 KV heads is checked
+bit for bit against the C oracle, including a release / admission round.
+"""
+import numpy as np
+import pytest
+import torch
+
+from analysis_spec_b200 import _ops, workloads as W
+from analysis_spec_b200.opd_static_cache import OPDStaticCache, swap_remove_plan
+from analysis_spec_b200.tree_verification import PackedTree
+from oracle import oracle
+from tests.cpu_ops import _np
+from tests.test_attention_gpu import check
+
+pytestmark = pytest.mark.gpu
+
+
+def verify_layer(batch, hq, hkv, prefix, rows, seed):
+    """Queries, K/V views over a left-padded cache and the tree visibility of one verify layer."""
+    rng = np.random.RandomState(seed)
+    past = int(prefix.max())
+    parents, tokens = W.packed_trees(rng, batch, rows - 1, 6, 10)
+    pad = np.zeros((batch, past + rows), dtype=bool)
+    pad[:, :past] = W.left_padding(prefix, past)
+    gen = torch.Generator(device='cuda').manual_seed(seed)
+    q = (0.5 * torch.randn(batch, rows, hq * 128, device='cuda', generator=gen)).bfloat16()
+    q = q.view(batch, rows, hq, 128).transpose(1, 2)
+    cap = past + rows + 17
+    kp = (0.5 * torch.randn(batch, hkv, cap, 128, device='cuda', generator=gen)).bfloat16()
+    vp = (0.5 * torch.randn(batch, hkv, cap, 128, device='cuda', generator=gen)).bfloat16()
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(tokens).cuda(),
+                      torch.zeros(batch, rows, dtype=torch.long, device='cuda'), 6)
+    vis = tree.visibility(past, torch.from_numpy(pad).cuda())
+    visible = oracle.tree_visible(parents, past, 7, pad=pad)
+    return q, kp[:, :, :past + rows], vp[:, :, :past + rows], vis, visible
+
+
+def check_slices(q, k, v, out, visible, slices):
+    for sl in slices:
+        expect = oracle.attention(q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy(),
+                                  v[sl].float().cpu().numpy(), oracle.additive_mask(visible[sl], 'bfloat16'),
+                                  128 ** -0.5)
+        check(out[sl], expect)
+
+
+def test_qwen25_7b_attention_long_prefixes():
+    """28 q / 4 KV heads (7 query heads per KV head), prefixes U{512..6144}, 61 tree rows."""
+    rng = np.random.RandomState(21)
+    batch = 32
+    prefix = W.prefix_lengths(rng, ('uniform', 512, 6144), batch)
+    prefix[3] = 6144
+    q, k, v, vis, visible = verify_layer(batch, 28, 4, prefix, 61, 21)
+    out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    longest = int(np.argmax(prefix))
+    check_slices(q, k, v, out, visible, (slice(longest, longest + 1), slice(0, 2), slice(batch - 1, batch)))
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
+@pytest.mark.parametrize('kv_len', [14061, 16300])
+def test_qwen25_14b_attention_near_capacity(kv_len):
+    """40 q / 8 KV heads (5 query heads per KV head), one sequence at kv_len columns beside
+    log-uniform shorter ones in the same left-padded cache."""
+    rng = np.random.RandomState(kv_len)
+    batch, rows = 6, 61
+    prefix = W.prefix_lengths(rng, ('loguniform', 128, 14000), batch)
+    prefix[2] = kv_len - rows
+    q, k, v, vis, visible = verify_layer(batch, 40, 8, prefix, rows, kv_len)
+    out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    check_slices(q, k, v, out, visible, (slice(2, 3), slice(0, 1), slice(5, 6)))
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
+def test_qwen25_14b_commit_release_admit_48_layers():
+    """48 layers x 8 KV heads x 128, 16 sequences: append 61 tree rows, compact accepted paths,
+    release a quarter of the sequences (swap_remove) and admit as many; every pool byte equals
+    the C oracle's result of the same operations."""
+    layers, b, h, d, past, rows, width = 48, 16, 8, 128, 700, 61, 7
+    gen = torch.Generator(device='cuda').manual_seed(48)
+    rng = np.random.RandomState(48)
+    cache = OPDStaticCache(1024, batch_capacity=b)
+    prefix = (0.5 * torch.randn(b, h, past, d, device='cuda', generator=gen)).bfloat16()
+    for l in range(layers):
+        cache.update(prefix, prefix, l)
+    tk = [(0.5 * torch.randn(b, rows, h * d, device='cuda', generator=gen)).bfloat16().view(b, rows, h, d)
+          .transpose(1, 2) for _ in range(2)]
+    tv = [(0.5 * torch.randn(b, rows, h * d, device='cuda', generator=gen)).bfloat16().view(b, rows, h, d)
+          .transpose(1, 2) for _ in range(2)]
+    cache.update_layers([tk[l % 2] for l in range(layers)], [tv[l % 2] for l in range(layers)])
+    # oracle: the same bytes on the host
+    kp = [np.ascontiguousarray(_np(cache.layers[l].key_pool.cpu())) for l in (0, 1)]
+    vp = [np.ascontiguousarray(_np(cache.layers[l].value_pool.cpu())) for l in (0, 1)]
+    chosen = np.empty((b, width), dtype=np.int64)
+    for i in range(b):
+        n = rng.randint(1, width + 1)
+        idx = np.sort(rng.choice(np.arange(1, rows), size=n - 1, replace=False)) if n > 1 else np.array([], int)
+        idx = np.concatenate([[0], idx])
+        slot = np.arange(width)
+        chosen[i] = past + np.where(slot < n, np.concatenate([idx, np.zeros(width - n, int)]), slot)
+    ext = 1
+    cache.commit_accepted(torch.from_numpy(chosen).cuda(), past, ext)
+    for l in (0, 1):
+        oracle.compact_suffix(kp[l], vp[l], b, past + rows, chosen, past, ext)
+    finished = [bool(x) for x in rng.rand(b) < 0.25]
+    finished[0] = True
+    keep, sources, holes = swap_remove_plan(finished)
+    cache.swap_remove(len(keep), torch.tensor(sources, device='cuda'), torch.tensor(holes, device='cuda'))
+    length = past + width
+    for l in (0, 1):
+        oracle.move_rows(kp[l], vp[l], np.array(sources, dtype=np.int64), np.array(holes, dtype=np.int64), length)
+    fresh = (0.5 * torch.randn(b - len(keep), h, length, d, device='cuda', generator=gen)).bfloat16()
+    cache.admit([fresh] * layers, [fresh] * layers)
+    fresh_np = np.ascontiguousarray(_np(fresh.cpu()))
+    for l in (0, 1):
+        kp[l][len(keep):b, :, :length] = fresh_np
+        vp[l][len(keep):b, :, :length] = fresh_np
+    for l in range(layers):
+        ref = l % 2
+        got_k = np.ascontiguousarray(_np(cache.layers[l].key_pool.cpu()))[:b, :, :length]
+        got_v = np.ascontiguousarray(_np(cache.layers[l].value_pool.cpu()))[:b, :, :length]
+        assert np.array_equal(got_k, kp[ref][:b, :, :length]), l
+        assert np.array_equal(got_v, vp[ref][:b, :, :length]), l
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
