@@ -643,6 +643,11 @@ def history_pack(dst, pool, offsets, rows, max_length):
               int(max_length), _stream(pool))
 
 
+def set_attention_ctas(ctas):
+    """Caps the persistent attention grid of this process at `ctas` CTAs (0: one per SM)."""
+    _lib.call('speckv_attention_set_ctas', int(ctas))
+
+
 @_on_device
 def acceptance_counts(packet, batch, proposed_per_row, counts):
     """counts[:5] = the round's acceptance-counter increments from the packet rows (device)."""

@@ -138,6 +138,12 @@ extern "C" int speckv_attention_launches(int64_t* tensor_core, int64_t* cuda_cor
   return SPECKV_OK;
 }
 
+extern "C" int speckv_attention_set_ctas(int32_t ctas) {
+  if (ctas < 0) return fail(SPECKV_EINVAL, "speckv_attention_set_ctas: negative CTA count");
+  attention_set_ctas(ctas);
+  return SPECKV_OK;
+}
+
 extern "C" int speckv_attention_test_hooks(int64_t wait_limit_ns, int32_t withhold_q_arrival) {
   if (wait_limit_ns < 0 || withhold_q_arrival < 0 || withhold_q_arrival > 1)
     return fail(SPECKV_EINVAL, "speckv_attention_test_hooks: wait limit >= 0 and a 0 / 1 switch expected");

@@ -35,4 +35,7 @@ int attention_sm100(const AttnArgs& a, cudaStream_t s);
 // visibility-bits kernel withholds its first Q-tile arrival.
 int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival);
 
+// Upper bound on the persistent attention grid for this process (<= 0: one CTA per SM).
+void attention_set_ctas(int ctas);
+
 }  // namespace speckv

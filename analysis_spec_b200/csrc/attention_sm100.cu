@@ -1452,6 +1452,10 @@ int current_device() {
   return cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxAttnDevices ? dev : -1;
 }
 
+// Upper bound on the persistent attention grid (0: one CTA per SM). A job whose collectives run
+// beside the attention (a counter all_reduce on a side stream) leaves their SMs free with it.
+int g_attention_ctas = 0;
+
 int sm_count() {
   static int cached[kMaxAttnDevices] = {0};
   const int dev = current_device();
@@ -1485,12 +1489,16 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   const long long qrows = BM / s.group, mtiles = (s.rows + qrows - 1) / qrows;
   const long long pairs = SPLIT ? 1 : (mtiles + 1) / 2;
   const long long items = (long long)s.batch * s.kv_heads * pairs;
-  const long long grid = items < sm_count() ? items : sm_count();
+  long long ctas = sm_count();
+  if (g_attention_ctas > 0 && g_attention_ctas < ctas) ctas = g_attention_ctas;
+  const long long grid = items < ctas ? items : ctas;
   kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, mq, s, kvr);
   return check_launch("speckv_tree_attention_bits(sm100)");
 }
 
 }  // namespace
+
+void attention_set_ctas(int ctas) { g_attention_ctas = ctas > 0 ? ctas : 0; }
 
 int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival) {
   const unsigned long long lim = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : 0ull;

@@ -382,20 +382,26 @@ def run_ours(args):
     device = torch.device('cuda', local)
     if world > 1:
         from datetime import timedelta
+        # the job's only collective is a 40-byte counter all_reduce: one NCCL CTA, and the
+        # persistent attention leaves that SM free (it runs beside it on a side stream)
+        os.environ.setdefault('NCCL_MAX_CTAS', '1')
         dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
     _lib.load()
+    if world > 1:
+        from analysis_spec_b200 import _ops
+        _ops.set_attention_ctas(torch.cuda.get_device_properties(device).multi_processor_count -
+                                int(os.environ['NCCL_MAX_CTAS']))
     wl = workload(args)
     st = Round(wl, device, seed=1000 + rank)
     counters = AcceptanceCounters(device)
     st.counters = counters
 
-    host_totals = [0] * 5  # the same increments summed from the host packet rows, as a check
+    round_rows = []  # the host packet rows of every round, summed after the timed region as a check
 
     def reduce_counters(rows):
         # increments computed on the device from the packet; the all_reduce runs on a side stream
         counters.add_device_round(st.packet, wl.batch, wl.nodes)
-        for k, v in enumerate(round_increments(rows, wl.nodes)):
-            host_totals[k] += v
+        round_rows.append(rows)
 
     for i in range(args.warmup):
         _, _, rows = verify_round(st, i)
@@ -428,6 +434,10 @@ def run_ours(args):
     launches = _lib.profile.calls + (args.steps * wl.layers if not args.no_graph else 0)
     kernel_ms = {name: [s.elapsed_time(e) for s, e in pairs] for name, pairs in _lib.profile.events.items()}
     totals = counters.finish()
+    host_totals = [0] * 5
+    for rows in round_rows:
+        for k, v in enumerate(round_increments(rows, wl.nodes)):
+            host_totals[k] += v
     if world > 1:  # the device totals are job-wide: sum the host check over the ranks too
         check = torch.tensor(host_totals, dtype=torch.long, device=device)
         dist.all_reduce(check)
@@ -937,8 +947,12 @@ def run_rollout(args):
     device = torch.device('cuda', local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault('NCCL_MAX_CTAS', '1')  # see run_ours
         dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
     _lib.load()
+    if world > 1:
+        _ops.set_attention_ctas(torch.cuda.get_device_properties(device).multi_processor_count -
+                                int(os.environ['NCCL_MAX_CTAS']))
     wl = workload(args)
     st = Round(wl, device, seed=1000 + rank, row_table=args.row_table)
     counters = AcceptanceCounters(device)

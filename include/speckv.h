@@ -446,6 +446,13 @@ int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
  * counterpart (the reference dispatches inside torch's SDPA). */
 int speckv_attention_launches(int64_t* tensor_core, int64_t* cuda_core);
 
+/* Upper bound on the persistent grid of speckv_tree_attention_bits for this process
+ * (0, the default: one CTA per SM). A job that runs a collective beside the attention
+ * (the sequence-sharded verify loop's counter all_reduce on a side stream) sets it to the
+ * SM count minus the collective's CTAs, so that no attention CTA waits for an SM the
+ * collective holds while it waits for the other ranks. No reference counterpart. */
+int speckv_attention_set_ctas(int32_t ctas);
+
 /* Test hook of the tensor-core attention kernels on the current device
  * (synchronous): every bounded wait inside them gives up after wait_limit_ns
  * (0 = the default of 2 s) and records SPECKV_DERR_TIMEOUT with the wait site;
