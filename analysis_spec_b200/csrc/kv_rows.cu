@@ -356,6 +356,10 @@ struct RoundGeom {
   PositionArgs pos;          // positions == null: no position update
 };
 
+// Round width and extension are reduced from the packet by warp 0 while every warp already
+// loads its group's rows: the chosen positions and rows of all max_width slots are read
+// speculatively (a slot outside [extension, width) is simply not stored), so the packet
+// reduction, the index load and the row load are not three dependent round trips.
 template <int V, int MAXR>
 __global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools, RoundGeom g,
                                                                 unsigned long long* err) {
@@ -363,10 +367,42 @@ __global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools,
   __shared__ int s_width, s_ext;
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t warp = threadIdx.x >> 5;
+  const bool compact = blockIdx.x < g.compact_blocks;
+  const uint32_t group = blockIdx.x * (kThreads / 32) + warp;
+  // speculative loads of this warp's group (compaction blocks only)
+  T buf[MAXR];
+  long long src[MAXR];  // source position, -1 = not loaded
+  char* base = nullptr;
+  uint32_t b = 0;
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) src[r] = -1;
+  if (compact && group < g.c.groups) {
+    uint32_t tensor, bh, h;
+    g.c.bh.divmod(group, tensor, bh);
+    g.c.heads.divmod(bh, b, h);
+    const long long pb = phys_row(g.c.rt, b, err);
+    if (pb >= 0) {
+      base = pools.ptr[tensor] + pb * g.c.sb + (long long)h * g.c.sh;
+      const uint32_t nv = g.max_width * g.c.nvec.d;
+#pragma unroll
+      for (int r = 0; r < MAXR; ++r) {
+        const uint32_t i = lane + r * 32;
+        if (i < nv) {
+          uint32_t j, lv;
+          g.c.nvec.divmod(i, j, lv);
+          const long long pos = g.chosen[(long long)b * g.c.csb + (long long)j * g.c.csw];
+          if (pos >= 0 && pos < g.c.length) {  // out of range: reported at the store if committed
+            src[r] = pos;
+            buf[r] = load_vec<V>(base + pos * g.c.row_bytes + (long long)lv * V);
+          }
+        }
+      }
+    }
+  }
   if (warp == 0) {
     long long wmax = 0, emin = LLONG_MAX;
-    for (uint32_t b = lane; b < g.batch; b += 32) {
-      const int64_t* row = g.packet + (long long)b * g.ps;
+    for (uint32_t bb = lane; bb < g.batch; bb += 32) {
+      const int64_t* row = g.packet + (long long)bb * g.ps;
       const long long len = row[0];
       wmax = len > wmax ? len : wmax;
       if (row[1] == 0 && row[2] < emin) emin = row[2];
@@ -389,47 +425,25 @@ __global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools,
   __syncthreads();
   const int width = s_width, ext = s_ext;
   if (width < 0) return;
-  if (blockIdx.x >= g.compact_blocks) {
-    const long long b = (long long)(blockIdx.x - g.compact_blocks) * (kThreads / 32) + warp;
-    if (b < g.batch && width > 0) position_row(g.pos, b, g.c.past, width, lane, err);
+  if (!compact) {
+    const long long bp = (long long)(blockIdx.x - g.compact_blocks) * (kThreads / 32) + warp;
+    if (bp < g.batch && width > 0) position_row(g.pos, bp, g.c.past, width, lane, err);
     return;
   }
-  const uint32_t group = blockIdx.x * (kThreads / 32) + warp;
-  if (group >= g.c.groups) return;
-  uint32_t tensor, bh, b, h;
-  g.c.bh.divmod(group, tensor, bh);
-  g.c.heads.divmod(bh, b, h);
-  const long long pb = phys_row(g.c.rt, b, err);
-  if (pb < 0) return;  // the whole warp shares b
-  char* base = pools.ptr[tensor] + pb * g.c.sb + (long long)h * g.c.sh;
-  const uint32_t nv = (uint32_t)(width - ext) * g.c.nvec.d;
-  T buf[MAXR];
-  int src[MAXR];  // source position, -1 = skipped (length < 2^31 is checked on the host)
+  if (base == nullptr) return;  // beyond the groups, or a row-table entry out of range (recorded)
+  // every read of this group happened above, before any write: overlapping slots are safe
 #pragma unroll
   for (int r = 0; r < MAXR; ++r) {
     const uint32_t i = lane + r * 32;
-    src[r] = -1;
-    if (i < nv) {
-      uint32_t j, lv;
-      g.c.nvec.divmod(i, j, lv);
-      const long long pos = g.chosen[(long long)b * g.c.csb + (long long)(ext + j) * g.c.csw];
-      if (pos < 0 || pos >= g.c.length) {
-        record_error(err, SPECKV_DERR_COMPACT_INDEX, pos);
-      } else {
-        src[r] = (int)pos;
-        buf[r] = load_vec<V>(base + pos * g.c.row_bytes + (long long)lv * V);
-      }
+    uint32_t j, lv;
+    g.c.nvec.divmod(i, j, lv);
+    if ((int)j < ext || (int)j >= width || i >= g.max_width * g.c.nvec.d) continue;
+    if (src[r] < 0) {  // a slot of the committed range whose position is out of [0, length)
+      if (lv == 0)
+        record_error(err, SPECKV_DERR_COMPACT_INDEX, g.chosen[(long long)b * g.c.csb + (long long)j * g.c.csw]);
+      continue;
     }
-  }
-  __syncwarp();
-#pragma unroll
-  for (int r = 0; r < MAXR; ++r) {
-    const uint32_t i = lane + r * 32;
-    if (i < nv && src[r] >= 0) {
-      uint32_t j, lv;
-      g.c.nvec.divmod(i, j, lv);
-      store_vec<V>(base + (g.c.past + ext + j) * g.c.row_bytes + (long long)lv * V, buf[r]);
-    }
+    store_vec<V>(base + (g.c.past + j) * g.c.row_bytes + (long long)lv * V, buf[r]);
   }
 }
 
