@@ -37,6 +37,7 @@ Multi-GPU (torchrun): every rank owns its own batch of sequences (weak scaling)
 and one int64 acceptance-counter all_reduce runs per step on a side stream.
 """
 import argparse
+import hashlib
 import json
 import os
 import subprocess
@@ -97,17 +98,29 @@ def peaks():
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 'fallback'
 
 
-def dram_traffic(entry, layers):
+def dram_traffic(entry, layers, workload='qwen25_3b'):
     """DRAM bytes per launch of one of this path's kernels from the committed ncu capture
-    (scaled to `layers` where the traffic grows with the layer count), or None."""
+    (scaled to `layers` where the traffic grows with the layer count) and where the figure
+    comes from, or (None, reason). The capture records a hash of the kernel's source file; the
+    label says whether the source built here still matches it."""
     path = ROOT / 'profiles' / 'dram_traffic_qwen25_3b.json'
     if not path.exists():
-        return None
-    k = json.loads(path.read_text())['kernels'].get(entry)
+        return None, 'no ncu capture committed'
+    if workload != 'qwen25_3b':
+        return None, 'DRAM traffic captured on the qwen25_3b workload only'
+    d = json.loads(path.read_text())
+    k = d['kernels'].get(entry)
     if k is None:
-        return None
+        return None, 'kernel not in the ncu capture'
     per = k['dram_read_bytes'] + k['dram_write_bytes']
-    return int(per * (layers / k['captured_layers'] if k['scale'] != 1.0 else 1.0))
+    src = k.get('source')
+    now = hashlib.sha256((ROOT / src).read_bytes()).hexdigest()[:16] if src and (ROOT / src).exists() else None
+    same = now is not None and now == d.get('sources', {}).get(src)
+    label = (f'ncu dram__bytes_read+write of {k["kernel"]}, {k["captured_layers"]}-layer capture scaled to '
+             f'{layers} layers' if k['scale'] != 1.0 else f'ncu dram__bytes_read+write of {k["kernel"]}, one launch')
+    label += ('; kernel source unchanged since the capture' if same else
+              '; kernel source CHANGED since the capture (figure is stale)')
+    return int(per * (layers / k['captured_layers'] if k['scale'] != 1.0 else 1.0)), label
 
 
 def workload_config(wl, extra=None):
@@ -476,6 +489,8 @@ def run_ours(args):
         kernel_ms['speckv_tree_attention_bits'] = [attn_launch_ms]
     attn_tflops = st.attention_flops() / wl.layers / (attn_launch_ms * 1e-3) / 1e12
     value = job_commit_bytes / (commit_ms * 1e-3) / 1e9
+    attn_traffic = dram_traffic('speckv_tree_attention_bits', wl.layers, wl.name)
+    append_traffic = dram_traffic('speckv_append_rows', wl.layers, wl.name)
     result = {
         'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
@@ -493,11 +508,11 @@ def run_ours(args):
                         'attention_tflops': round(attn_tflops, 2),
                         'roofline': {'bound': 'tensor', 'achieved': round(attn_tflops, 2), 'peak': tflops,
                                      'unit': 'TFLOP/s', 'frac': round(attn_tflops / tflops, 4),
-                                     'traffic': dram_traffic('speckv_tree_attention_bits', wl.layers),
+                                     'traffic': attn_traffic[0], 'traffic_source': attn_traffic[1],
                                      'peak_kind': peak_kind}},
         'roofline': {'bound': 'hbm', 'kernel': 'speckv_append_rows (all layers)', 'achieved': round(append_gbs, 1),
                      'peak': hbm, 'unit': 'GB/s', 'frac': round(append_gbs / hbm, 4),
-                     'traffic': dram_traffic('speckv_append_rows', wl.layers),
+                     'traffic': append_traffic[0], 'traffic_source': append_traffic[1],
                      'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
         'gpu_launches': launches,
