@@ -64,7 +64,9 @@ def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
     if packet is None:
         packet = torch.empty((b, capacity + 4), device=path.tokens.device, dtype=torch.long)
     out_packet = packet[:b, :capacity + 3]
-    reflex = opd is not None and getattr(opd, 'enabled', True)
+    # as in the reference, the OPD runtime's active-count snapshot rides in the packet only on
+    # the plugin path; without a plugin `opd` is not read
+    reflex = kernels is not None and opd is not None and getattr(opd, 'enabled', True)
     snapshot = None
     if reflex:
         snapshot = (opd.dispatch_snapshot if getattr(opd, 'async_updates', False)
