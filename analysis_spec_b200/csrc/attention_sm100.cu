@@ -640,14 +640,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // that one 4-D TMA box (64 dims x g heads x q rows) fetches it from the strided
 // projection; rows q * g .. 127 stay zero (they are never written).
 //
-//   warp 0      TMA producer: the Q tiles of the next item (as soon as the last
-//               S MMA of the current item has read the Q buffer), then the K tiles
-//               of a 2-stage ring
+//   warp 3      TMA producer of the Q tiles: the next item's, as soon as the last S
+//               MMA of the current item has read the Q buffer
+//   warp 0      TMA producer of the K tiles (2-stage ring); prefetches the next item's
+//               first tiles into L2
 //   warp 2      TMA producer of the V tiles (2-stage ring)
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O0 | O1) + MMA issuer, order per
 //               key tile i: S0_i, P1_{i-1} V_{i-1}, S1_i, P0_i V_i, so each softmax
 //               warpgroup works while the tensor pipe serves the other tile
-//   warp 3      idle (it completes the first warpgroup for the register split)
 //   warps 4-7   softmax of row tile 0; warps 8-11 softmax of row tile 1: thread =
 //               row = TMEM lane (warp % 4 picks the lane quarter); S is read once
 //               into registers, P (16-bit) goes back into the first 64 columns of
@@ -907,22 +907,22 @@ __global__ void __launch_bounds__(kThreads2, 1)
 
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
-  if (warp == 0 || warp == 2) {
+  if (warp == 0 || warp == 2 || warp == 3) {
     // ---------------- TMA producers ----------------
-    // One thread issues TMA loads at about 50 GB/s, below what the K / V rings need, so
-    // two warps share the work: warp 0 loads the Q tiles and the K ring (and prefetches
-    // the next item into L2), warp 2 the V ring. Both walk the same item list.
+    // One thread issues TMA loads at about 50 GB/s (measured), below what an item start
+    // needs (two Q tiles and the first K and V tiles at once), so three warps share the
+    // work: warp 3 loads the Q tiles, warp 0 the K ring (and prefetches the next item into
+    // L2), warp 2 the V ring. All walk the same item list.
     if (lane == 0) {
-      const bool kq = warp == 0;
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(kq ? &tmk : &tmv)) : "memory");
-      if (kq) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
-      const CUtensorMap* map = kq ? &tmk : &tmv;
+      const bool kq = warp == 0, qw = warp == 3;
+      const CUtensorMap* map = qw ? &tmq : kq ? &tmk : &tmv;
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
       const int full0 = kq ? C_K_FULL : C_V_FULL, empty0 = kq ? C_K_EMPTY : C_V_EMPTY;
       const uint32_t ring = sbase + (kq ? K2_OFF : V2_OFF);
       int cnt = 0, issued = 0;
       int qc[2] = {0, 0};                 // Q tiles requested per row tile
       bool q_issued[2] = {false, false};  // the latest request was sent (not withheld)
-      const bool withhold = kq && blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0;
+      const bool withhold = qw && blockIdx.x == 0 && *reinterpret_cast<volatile int*>(&g_withhold_q_arrival) != 0;
       const uint32_t q_bytes = 2u * 128u * (uint32_t)(qrows * a.group);  // two 64-dim halves of q * g rows
       bool ok = true;
       Item it;
@@ -938,7 +938,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
         // Q tiles of the item: each buffer is free once the previous item's last S MMA has read it
-        const int ntq = !kq ? 0 : ((SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2);
+        const int ntq = !qw ? 0 : ((SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2);
         for (int t = 0; t < ntq; ++t) {
           if (qc[t] >= 1 && !mbar_wait(bar(C_Q_EMPTY + t), (qc[t] - 1) & 1, abort_flag, a.err, 20)) { ok = false; break; }
           ++qc[t];
@@ -951,6 +951,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
           tma_load_4d(qd + kTileHalf, &tmq, bar(C_Q_FULL + t), 64, it.kvh * a.group, r0, it.b);
         }
         if (!ok) break;
+        if (qw) continue;  // warp 3 loads only the Q tiles
         const int t0 = tile0_of(it.b);
         const int kb = kv_row(it.b, kq);
         // three key tiles before this item ends, the next item's Q tiles and first K / V

@@ -467,12 +467,19 @@ def run_ours(args):
     verify_ms = sum(ev[i][0].elapsed_time(ev[i][1]) + ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     attn_ms = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     commit_bytes = sum(st.append_bytes + st.compact_bytes(w, e) for w, e in widths)
-    times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms, region_ms], device=device, dtype=torch.float64)
+    # where a step's device time goes, per phase (ms per step): marks 0-4 of verify_round, and the
+    # time from a round's last mark to the next round's first one (host work between rounds,
+    # after the packet read-back, while the GPU has nothing queued)
+    phases = [sum(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(args.steps)) / args.steps for j in range(4)]
+    between = (sum(ev[i][4].elapsed_time(ev[i + 1][0]) for i in range(args.steps - 1)) / (args.steps - 1)
+               if args.steps > 1 else 0.0)
+    times = torch.tensor([total_ms, commit_ms, verify_ms, attn_ms, region_ms, *phases, between], device=device,
+                         dtype=torch.float64)
     moved = torch.tensor([float(commit_bytes)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(moved)
-    total_ms, commit_ms, verify_ms, attn_ms, region_ms = times.tolist()
+    total_ms, commit_ms, verify_ms, attn_ms, region_ms, *phases, between = times.tolist()
     job_commit_bytes = moved.item()
 
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
@@ -515,6 +522,9 @@ def run_ours(args):
                      'traffic': append_traffic[0], 'traffic_source': append_traffic[1],
                      'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
+        'step_phases_ms': {'visibility': round(phases[0], 4), 'append': round(phases[1], 4),
+                           'attention': round(phases[2], 4), 'trace_schedule_commit_readback': round(phases[3], 4),
+                           'between_rounds': round(between, 4), 'max_over_ranks': True},
         'gpu_launches': launches,
         'attention_launches': attention_launches(),
         'acceptance': totals,
