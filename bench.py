@@ -537,6 +537,7 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(wl, budget_s=10.0)
         result['cpu_baseline_c_port'] = c_port_baseline(wl, budget_s=6.0)
+        result['cpu_baseline_attention'] = cpu_attention_baseline(wl, budget_s=6.0)
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
@@ -918,6 +919,44 @@ def cpu_baseline(wl, budget_s=10.0):
     dt = time.perf_counter() - t0
     return {'value': round(moved / dt / 1e9, 4), 'unit': 'GB/s', 'cores': torch.get_num_threads(), 'kind': 'port',
             'sample': torch_commit_sample(wl, rounds) + f', {dt:.1f} s'}
+
+
+def cpu_attention_baseline(wl, budget_s=6.0):
+    """The reference's tree-verify attention on the host cores: transformers'
+    sdpa_attention_forward (repeat_kv of K / V, then torch's scaled_dot_product_attention with
+    the dense additive tree mask; the call the reference's verify forward makes) over one layer
+    of a bounded sample of the workload's sequences, in the workload's dtype. TFLOP/s counts the
+    same algorithmic flops as the GPU figure (4 Hq R (P + R) D per sequence)."""
+    import torch
+    from types import SimpleNamespace
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    from analysis_spec_b200 import workloads as W
+    from oracle import oracle
+    rng = np.random.RandomState(1000)
+    prefix = W.prefix_lengths(rng, wl.prefix, wl.batch)
+    parents, _ = W.packed_trees(rng, wl.batch, wl.nodes, wl.depth, wl.topk)
+    dtype = getattr(torch, wl.dtype)
+    g = torch.Generator().manual_seed(3)
+    module = SimpleNamespace(num_key_value_groups=wl.q_heads // wl.kv_heads, is_causal=True, training=False)
+    flops, calls, t_all = 0, 0, 0.0
+    order = np.argsort(-prefix)  # the sample walks the sequences longest first, then wraps
+    while t_all < budget_s:
+        b = int(order[calls % wl.batch])
+        p = int(prefix[b])
+        q = (0.5 * torch.randn(1, wl.q_heads, wl.rows, wl.dim, generator=g)).to(dtype)
+        k = (0.5 * torch.randn(1, wl.kv_heads, p + wl.rows, wl.dim, generator=g)).to(dtype)
+        v = (0.5 * torch.randn(1, wl.kv_heads, p + wl.rows, wl.dim, generator=g)).to(dtype)
+        vis = oracle.tree_visible(parents[b:b + 1], p, wl.depth + 1)
+        mask = torch.from_numpy(np.where(vis, 0.0, np.float32(torch.finfo(dtype).min))).to(dtype)[:, None]
+        t0 = time.perf_counter()
+        sdpa_attention_forward(module, q, k, v, mask, dropout=0.0, scaling=wl.dim ** -0.5)
+        t_all += time.perf_counter() - t0
+        flops += 4 * wl.q_heads * wl.rows * (p + wl.rows) * wl.dim
+        calls += 1
+    return {'value': round(flops / t_all / 1e12, 5), 'unit': 'TFLOP/s', 'cores': torch.get_num_threads(),
+            'kind': 'reference',
+            'sample': f'{calls} single-sequence verify layers (longest prefixes first) through transformers '
+                      f'sdpa_attention_forward on the host cores, {wl.dtype}, {t_all:.1f} s'}
 
 
 def run_reference(args):
