@@ -60,6 +60,7 @@ SIGNATURES = {
     'speckv_attention_test_hooks': [_i64, _i32],
     'speckv_acceptance_counts': [_p, _i64, _i64, _i64, _p, _p],
     'speckv_attention_set_ctas': [_i32],
+    'speckv_attention_set_chunks': [_i32],
 }
 
 # entries with a prepare / launch split (speckv_<name>_prepare + speckv_plan_launch)

@@ -648,6 +648,12 @@ def set_attention_ctas(ctas):
     _lib.call('speckv_attention_set_ctas', int(ctas))
 
 
+def set_attention_chunks(on):
+    """Turns key-range chunks of long sequences in the visibility-bits attention on or off for
+    this process (off by default): for batches of ragged long sequences."""
+    _lib.call('speckv_attention_set_chunks', 1 if on else 0)
+
+
 @_on_device
 def acceptance_counts(packet, batch, proposed_per_row, counts):
     """counts[:5] = the round's acceptance-counter increments from the packet rows (device)."""

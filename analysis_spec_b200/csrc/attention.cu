@@ -144,6 +144,12 @@ extern "C" int speckv_attention_set_ctas(int32_t ctas) {
   return SPECKV_OK;
 }
 
+extern "C" int speckv_attention_set_chunks(int32_t on) {
+  if (on < 0 || on > 1) return fail(SPECKV_EINVAL, "speckv_attention_set_chunks: 0 or 1 expected");
+  attention_set_chunks(on);
+  return SPECKV_OK;
+}
+
 extern "C" int speckv_attention_test_hooks(int64_t wait_limit_ns, int32_t withhold_q_arrival) {
   if (wait_limit_ns < 0 || withhold_q_arrival < 0 || withhold_q_arrival > 1)
     return fail(SPECKV_EINVAL, "speckv_attention_test_hooks: wait limit >= 0 and a 0 / 1 switch expected");

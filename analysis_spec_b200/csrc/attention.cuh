@@ -38,4 +38,11 @@ int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival);
 // Upper bound on the persistent attention grid for this process (<= 0: one CTA per SM).
 void attention_set_ctas(int ctas);
 
+// Key-range chunks of long sequences in the visibility-bits kernel (0: off, the default).
+void attention_set_chunks(int on);
+
+// Zeroes the merge counters of split attention items (all slots): a launch leaves them at zero
+// when it completes; after a launch that ended in an error they may not be.
+int attention_reset_partials();
+
 }  // namespace speckv

@@ -27,6 +27,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -74,6 +76,22 @@ constexpr unsigned long long kWaitNs = 2000000000ull;
 __device__ unsigned long long g_wait_limit_ns = 0ull;
 __device__ int g_withhold_q_arrival = 0;
 
+// Key-range chunks (the pair kernel's CHUNKS form): when a sequence has more key tiles than a
+// CTA's average share of the launch, its items are split into chunks of about that share, and
+// each chunk leaves its partial result here: per launch slot, a merge counter per (sequence,
+// KV head, row tile) and the partial tiles, 128 rows of 128 unnormalised O values plus the
+// running max and sum (fp32, rows padded to 132 floats). The warpgroup that finishes a row
+// tile's last chunk merges the partials, writes the output and zeroes the counter; launches
+// that may run at the same time take different slots.
+constexpr int kPartSlots = 4;
+constexpr int kPartCounters = 1 << 16;
+constexpr int kPartTiles = 240;
+constexpr int kPartRowFloats = 132;
+constexpr int kPartTileFloats = 128 * kPartRowFloats;
+constexpr int kMaxChunks = 8;
+__device__ int g_part_count[kPartSlots * kPartCounters];
+__device__ __align__(16) float g_part[(size_t)kPartSlots * kPartTiles * kPartTileFloats];
+
 __device__ __forceinline__ unsigned long long wait_limit() {
   const unsigned long long v = *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
   return v != 0ull ? v : kWaitNs;
@@ -94,6 +112,7 @@ struct Sm100Args {
   int mask_dtype;
   int batch, q_heads, kv_heads, group, rows, kv_len, mtiles;
   float scale_log2;       // softmax scale * log2(e)
+  int part_slot;          // pair kernel with key-range chunks: slot of this launch's partials
   unsigned long long* err;
 };
 
@@ -673,12 +692,30 @@ constexpr uint32_t KEY2_OFF = 6 * kTileBytes;     // int keys[kMaxSortB]
 constexpr uint32_t ORD2_OFF = KEY2_OFF + 4 * kMaxSortB;  // int order[kMaxSortB]
 constexpr uint32_t BAR2_OFF = ORD2_OFF + 4 * kMaxSortB;
 constexpr uint32_t SMEM2_BYTES = BAR2_OFF + 256 + 1024;
+// the CHUNKS form adds, past the end of the common layout: start[kMaxSortB + 2] (first item of
+// each rank), pbase[kMaxSortB] (first partial tile of each sequence), cinfo[kMaxSortB] (chunk
+// length | chunk count << 16 of each sequence)
+constexpr uint32_t START2_OFF = BAR2_OFF + 256;
+constexpr uint32_t PBASE2_OFF = START2_OFF + 4 * (kMaxSortB + 2);
+constexpr uint32_t CINFO2_OFF = PBASE2_OFF + 4 * kMaxSortB;
+constexpr uint32_t SMEM2C_BYTES = CINFO2_OFF + 4 * kMaxSortB + 1024;
+static_assert(SMEM2C_BYTES <= 232448, "shared memory of the CHUNKS form");
 __host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * 128u; }
 __host__ __device__ constexpr uint32_t O2_COL(int t) { return 256u + (uint32_t)t * 128u; }
 
 enum { C_K_FULL = 0, C_K_EMPTY = 2, C_V_FULL = 4, C_V_EMPTY = 6, C_S_FULL = 8, C_O_FINAL = 10, C_Q_FULL = 12,
        C_P_FULL = 14, C_DRAIN = 16, C_ABORT = 17, C_TMEM_SLOT = 18, C_XCHG = 19, C_Q_EMPTY = 20, C_O_READ = 22,
-       C_PH_FULL = 24 };
+       C_PH_FULL = 24, C_PLAN = 26, C_LAST = 28 };
+static_assert(8 * (C_LAST + 1) <= 256, "barrier area");
+
+// Key-range split of a sequence of n key tiles for a target of `avg` tiles per chunk: the
+// chunk length and the number of (non-empty) chunks.
+__host__ __device__ inline void split_of(int n, int avg, int& len, int& nch) {
+  int n0 = n > avg ? (n + avg - 1) / avg : 1;
+  n0 = n0 < kMaxChunks ? n0 : kMaxChunks;
+  len = (n + n0 - 1) / n0;
+  nch = (n + len - 1) / len;
+}
 
 // Warp-wide forms: every lane runs the same code (the operands stay warp-uniform) and
 // one elected lane, always lane 0 with the full mask, issues the instruction; the
@@ -801,7 +838,7 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 __host__ __device__ constexpr bool poly_pair(int q) { return (q & 7) == 1 || (q & 7) == 5; }
 
 struct Item {
-  int b, kvh, pair;
+  int b, kvh, pair;  // CHUNKS: pair holds the row-tile pair in bits 0-15 and the key-range chunk above
 };
 
 // SPLIT (at most 128 packed rows per (sequence, KV head), e.g. a draft step): both
@@ -812,7 +849,7 @@ struct Item {
 // and then signals C_O_READ: the next item's first P.V waits for it.
 // TABLE: the K/V rows of sequence b come from a.row_table[b] (a separate instantiation, so
 // the table-free kernel carries no trace of it).
-template <typename T, bool SPLIT, bool TABLE>
+template <typename T, bool SPLIT, bool TABLE, bool CHUNKS>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const __grid_constant__ CUtensorMap tmq, const Sm100Args a, const KvRows kvr) {
@@ -825,13 +862,19 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BAR2_OFF + 8 * C_TMEM_SLOT);
   int* keys = reinterpret_cast<int*>(smem + KEY2_OFF);
   int* order = reinterpret_cast<int*>(smem + ORD2_OFF);
+  // CHUNKS only (unused otherwise)
+  int* start = reinterpret_cast<int*>(smem + START2_OFF);
+  int* pbase = reinterpret_cast<int*>(smem + PBASE2_OFF);
+  int* cinfo = reinterpret_cast<int*>(smem + CINFO2_OFF);
+  int* plan = reinterpret_cast<int*>(smem + BAR2_OFF + 8 * C_PLAN);  // tile sum, tile maximum
+  volatile int* lastf = reinterpret_cast<volatile int*>(smem + BAR2_OFF + 8 * C_LAST);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qrows = BM / a.group;                        // whole tree rows per 128-row tile
   const int mtiles = (a.rows + qrows - 1) / qrows;       // row tiles per (sequence, KV head)
   const int pairs = SPLIT ? 1 : (mtiles + 1) / 2;
   const int per_b = a.kv_heads * pairs;
-  const int n_items = a.batch * per_b;
+  int n_items = a.batch * per_b;
   const int n_tiles_all = (a.kv_len + BN - 1) / BN;
   const bool sorted = a.batch <= kMaxSortB;
   auto first_tile = [&](int b) {
@@ -852,6 +895,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       mbar_init(bar(C_Q_EMPTY + i), 1);
       mbar_init(bar(C_P_FULL + i), 128);
       mbar_init(bar(C_PH_FULL + i), 128);
+    }
+    if (CHUNKS) {  // tile sum and maximum over the sequences, accumulated by the sort below
+      plan[0] = 0;
+      plan[1] = 0;
     }
     mbar_init(bar(C_DRAIN), 1);
     mbar_init(bar(C_XCHG), 128);
@@ -885,11 +932,43 @@ __global__ void __launch_bounds__(kThreads2, 1)
       int rank = 0;
       for (int o = 0; o < a.batch; ++o) rank += (keys[o] > k) || (keys[o] == k && o < b);
       order[rank] = b;
+      if (CHUNKS) {
+        atomicAdd(plan, k);
+        atomicMax(plan + 1, k);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // CHUNKS: when a sequence has more key tiles than a CTA's average share of the launch (tile
+  // sum x items per sequence / grid), its items are split into key-range chunks of about that
+  // share. Every CTA derives the same plan from the same keys.
+  int split_avg = 0;
+  bool chunks = false;
+  if (CHUNKS && sorted) {
+    split_avg = (int)(((long long)plan[0] * per_b + gridDim.x - 1) / gridDim.x);
+    if (split_avg >= 1 && plan[1] > split_avg && (long long)a.batch * a.kv_heads * mtiles <= kPartCounters) {
+      if (threadIdx.x == 0) {
+        int n = 0, parts = 0;
+        for (int r = 0; r < a.batch; ++r) {
+          const int b = order[r];
+          int len, nch;
+          split_of(keys[b], split_avg, len, nch);
+          start[r] = n;
+          pbase[b] = parts;
+          cinfo[b] = len | (nch << 16);
+          n += per_b * nch;
+          if (nch > 1) parts += a.kv_heads * mtiles * nch;
+        }
+        start[a.batch] = n;
+        start[a.batch + 1] = parts <= kPartTiles ? 1 : 0;
+      }
+      __syncthreads();
+      chunks = start[a.batch + 1] != 0;
+      if (chunks) n_items = start[a.batch];
+    }
+  }
   const uint32_t tmem = *tmem_slot;
   // first key tile of sequence b, from the sort keys in shared memory when they exist
   auto tile0_of = [&](int b) { return sorted ? n_tiles_all - keys[b] : first_tile(b); };
@@ -898,11 +977,38 @@ __global__ void __launch_bounds__(kThreads2, 1)
   auto item_at = [&](int k, Item& it) -> bool {
     const int p = k * G + ((k & 1) ? (G - 1 - c) : c);
     if (p >= n_items) return false;
-    const int rank = p / per_b, rem = p % per_b;
-    it.b = sorted ? order[rank] : rank;
+    if (!CHUNKS || !chunks) {
+      const int rank = p / per_b, rem = p % per_b;
+      it.b = sorted ? order[rank] : rank;
+      it.kvh = rem / pairs;
+      it.pair = rem % pairs;
+      return true;
+    }
+    int lo = 0, hi = a.batch;  // start[lo] <= p < start[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (start[mid] <= p) lo = mid;
+      else hi = mid;
+    }
+    it.b = order[lo];
+    int rem = p - start[lo];
+    const int nch = cinfo[it.b] >> 16;
+    const int chunk = rem % nch;
+    rem /= nch;
     it.kvh = rem / pairs;
-    it.pair = rem % pairs;
+    it.pair = (rem % pairs) | (chunk << 16);
     return true;
+  };
+  // row-tile pair of an item, and its key tiles [lo, hi)
+  auto pair_of = [&](const Item& x) { return CHUNKS ? (x.pair & 0xffff) : x.pair; };
+  auto range_of = [&](const Item& x, int& lo, int& hi) {
+    lo = tile0_of(x.b);
+    hi = n_tiles_all;
+    if (CHUNKS && chunks) {
+      const int len = cinfo[x.b] & 0xffff;
+      lo += (x.pair >> 16) * len;
+      hi = min(hi, lo + len);
+    }
   };
 
   if (warp < 4) {
@@ -938,35 +1044,38 @@ __global__ void __launch_bounds__(kThreads2, 1)
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
         // Q tiles of the item: each buffer is free once the previous item's last S MMA has read it
-        const int ntq = !qw ? 0 : ((SPLIT || it.pair * 2 + 1 >= mtiles) ? 1 : 2);
+        const int ntq = !qw ? 0 : ((SPLIT || pair_of(it) * 2 + 1 >= mtiles) ? 1 : 2);
         for (int t = 0; t < ntq; ++t) {
           if (qc[t] >= 1 && !mbar_wait(bar(C_Q_EMPTY + t), (qc[t] - 1) & 1, abort_flag, a.err, 20)) { ok = false; break; }
           ++qc[t];
           q_issued[t] = !(withhold && k == 0 && t == 0);  // test hook: this tile never arrives
           if (!q_issued[t]) continue;
           const uint32_t qd = sbase + Q2_OFF + t * kTileBytes;
-          const int r0 = SPLIT ? 0 : (it.pair * 2 + t) * qrows;
+          const int r0 = SPLIT ? 0 : (pair_of(it) * 2 + t) * qrows;
           mbar_expect_tx(bar(C_Q_FULL + t), q_bytes);
           tma_load_4d(qd, &tmq, bar(C_Q_FULL + t), 0, it.kvh * a.group, r0, it.b);
           tma_load_4d(qd + kTileHalf, &tmq, bar(C_Q_FULL + t), 64, it.kvh * a.group, r0, it.b);
         }
         if (!ok) break;
         if (qw) continue;  // warp 3 loads only the Q tiles
-        const int t0 = tile0_of(it.b);
+        int t0, t1;
+        range_of(it, t0, t1);
         const int kb = kv_row(it.b, kq);
         // three key tiles before this item ends, the next item's Q tiles and first K / V
         // tiles are prefetched into L2, so that its start does not wait on DRAM
-        const int prefetch_at = max(t0, n_tiles_all - 3);
-        for (int i = t0; i < n_tiles_all; ++i, ++cnt) {
+        const int prefetch_at = max(t0, t1 - 3);
+        for (int i = t0; i < t1; ++i, ++cnt) {
           const int s = cnt & 1;
           Item nx;
           if (kq && i == prefetch_at && item_at(k + 1, nx)) {
-            const int nq = (SPLIT || nx.pair * 2 + 1 >= mtiles) ? 1 : 2;
+            const int nq = (SPLIT || pair_of(nx) * 2 + 1 >= mtiles) ? 1 : 2;
             for (int t = 0; t < nq; ++t)
               for (int h = 0; h < 2; ++h)
-                tma_prefetch_4d(&tmq, h * 64, nx.kvh * a.group, SPLIT ? 0 : (nx.pair * 2 + t) * qrows, nx.b);
-            const int nt0 = tile0_of(nx.b), nkb = kv_row(nx.b, false);
-            for (int j = nt0; j < nt0 + 2 && j < n_tiles_all; ++j)
+                tma_prefetch_4d(&tmq, h * 64, nx.kvh * a.group, SPLIT ? 0 : (pair_of(nx) * 2 + t) * qrows, nx.b);
+            int nt0, nt1;
+            range_of(nx, nt0, nt1);
+            const int nkb = kv_row(nx.b, false);
+            for (int j = nt0; j < nt0 + 2 && j < nt1; ++j)
               for (int h = 0; h < 2; ++h) {
                 tma_prefetch_4d(&tmk, h * 64, j * BN, nx.kvh, nkb);
                 tma_prefetch_4d(&tmv, h * 64, j * BN, nx.kvh, nkb);
@@ -1057,7 +1166,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       };
       for (int k = 0; ok && item_at(k, it); ++k) {
         if (SPLIT) {
-          const int n = n_tiles_all - tile0_of(it.b);
+          int r0, r1;
+          range_of(it, r0, r1);
+          const int n = r1 - r0;
           ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
           tc_fence_after();
           // O0 and O1 of the previous item must be read (merged) before this item's first P.V
@@ -1101,8 +1212,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
           ++ic[1];
           continue;
         }
-        const bool act1 = it.pair * 2 + 1 < mtiles;
-        const int n = n_tiles_all - tile0_of(it.b);
+        const bool act1 = pair_of(it) * 2 + 1 < mtiles;
+        int r0, r1;
+        range_of(it, r0, r1);
+        const int n = r1 - r0;
         ok = wait(C_Q_FULL + 0, ic[0] & 1, 24);
         if (ok && act1) ok = wait(C_Q_FULL + 1, ic[1] & 1, 25);
         tc_fence_after();
@@ -1161,7 +1274,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     // tile row -> (tree row, query head): the packing of the Q tensor map's boxes
     auto row_map = [&](const Item& x) {
       RowMap m;
-      const int tile = SPLIT ? 0 : x.pair * 2 + t;
+      const int tile = SPLIT ? 0 : pair_of(x) * 2 + t;
       const int rr = tile * qrows + row / a.group;
       m.valid = row < qrows * a.group && rr < a.rows;
       m.r = m.valid ? rr : 0;
@@ -1171,7 +1284,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     auto next_item = [&](int& kk, Item& nx) -> bool {
       for (;; ++kk) {
         if (!item_at(kk, nx)) return false;
-        if (SPLIT || t == 0 || nx.pair * 2 + 1 < mtiles) return true;
+        if (SPLIT || t == 0 || pair_of(nx) * 2 + 1 < mtiles) return true;
       }
     };
     const bool out32 = (reinterpret_cast<uintptr_t>(a.out) & 31u) == 0;  // 32-byte output stores
@@ -1181,8 +1294,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
     bool have = next_item(k, it);
     const int i_first = SPLIT ? t : 0, i_step = SPLIT ? 2 : 1;  // this warpgroup's key tiles
     while (have) {
-      const int t0 = tile0_of(it.b);
-      const int n = n_tiles_all - t0;
+      int t0, t1;
+      range_of(it, t0, t1);
+      const int n = t1 - t0;
       const RowMap m = row_map(it);
       const uint32_t* brow = a.bits + ((long long)it.b * a.rows + m.r) * a.row_words + t0 * 4;
       float m_run = -INFINITY, l_run = 0.f;
@@ -1275,6 +1389,81 @@ __global__ void __launch_bounds__(kThreads2, 1)
       ok = mbar_wait(bar(C_O_FINAL + t), ic & 1, abort_flag, a.err, 29);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
+      if (CHUNKS && !SPLIT && chunks && (cinfo[it.b] >> 16) > 1) {
+        // one chunk of a split row tile: its unnormalised O, running max and sum go to the
+        // launch's partials; the warpgroup that completes the tile's last chunk merges
+        ++ic;
+        const int nch = cinfo[it.b] >> 16;
+        const int tile = pair_of(it) * 2 + t, chunk = it.pair >> 16;
+        float* const parts = g_part + ((size_t)a.part_slot * kPartTiles + pbase[it.b] +
+                                       (it.kvh * mtiles + tile) * nch) * kPartTileFloats;
+        float* const prow = parts + (size_t)chunk * kPartTileFloats + row * kPartRowFloats;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          float o[32];
+          tmem_ld32(o_addr + cc * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            __stcg(reinterpret_cast<float4*>(prow + cc * 32 + j), make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]));
+        }
+        __stcg(reinterpret_cast<float2*>(prow + 128), make_float2(m_run, l_run));
+        tc_fence_before();
+        __threadfence();
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
+        int* const counter = g_part_count + (size_t)a.part_slot * kPartCounters +
+                             ((long long)it.b * a.kv_heads + it.kvh) * mtiles + tile;
+        if (row == 0) lastf[t] = atomicAdd(counter, 1) == nch - 1 ? 1 : 0;
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
+        if (lastf[t]) {
+          __threadfence();
+          const float* const rows0 = parts + row * kPartRowFloats;
+          float mm = -INFINITY;
+          for (int cc = 0; cc < nch; ++cc) mm = fmaxf(mm, __ldcg(rows0 + (size_t)cc * kPartTileFloats + 128));
+          float l = 0.f;
+          for (int cc = 0; cc < nch; ++cc) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(rows0 + (size_t)cc * kPartTileFloats + 128));
+            l += ml.x == -INFINITY ? 0.f : ml.y * ex2(ml.x - mm);
+          }
+          const float inv_l = l > 0.f ? 1.f / l : 0.f;
+          T* orow = static_cast<T*>(a.out) + (((long long)it.b * a.rows + m.r) * a.q_heads + m.hq) * HD;
+#pragma unroll 1
+          for (int cb = 0; cb < 4; ++cb) {
+            float acc[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+            for (int cc = 0; cc < nch; ++cc) {
+              const float* src = rows0 + (size_t)cc * kPartTileFloats;
+              const float mc = __ldcg(src + 128);
+              const float w = mc == -INFINITY ? 0.f : ex2(mc - mm) * inv_l;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(src + cb * 32 + j));
+                acc[j] += w * v.x;
+                acc[j + 1] += w * v.y;
+                acc[j + 2] += w * v.z;
+                acc[j + 3] += w * v.w;
+              }
+            }
+            if (m.valid) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 v;
+                v.x = pack2<T>(acc[j], acc[j + 1]);
+                v.y = pack2<T>(acc[j + 2], acc[j + 3]);
+                v.z = pack2<T>(acc[j + 4], acc[j + 5]);
+                v.w = pack2<T>(acc[j + 6], acc[j + 7]);
+                *reinterpret_cast<uint4*>(orow + cb * 32 + j) = v;
+              }
+            }
+          }
+          if (row == 0) atomicExch(counter, 0);  // ready for the slot's next launch
+        }
+        it = nx;
+        k = kn;
+        have = have_next;
+        continue;
+      }
       float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       float c0 = 1.f, c1 = 0.f;  // SPLIT: weights of O0 and O1 in the merged output
       bool use1 = false;
@@ -1457,6 +1646,9 @@ int current_device() {
 // beside the attention (a counter all_reduce on a side stream) leaves their SMs free with it.
 int g_attention_ctas = 0;
 
+// Key-range chunks for long sequences (speckv_attention_set_chunks): off by default.
+int g_attention_chunks = 0;
+
 int sm_count() {
   static int cached[kMaxAttnDevices] = {0};
   const int dev = current_device();
@@ -1467,10 +1659,11 @@ int sm_count() {
   return n;
 }
 
-template <typename T, bool SPLIT, bool TABLE>
+template <typename T, bool SPLIT, bool TABLE, bool CHUNKS = false>
 int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Sm100Args& s,
                 const KvRows& kvr, cudaStream_t stream) {
-  auto kern = attn_pair_kernel<T, SPLIT, TABLE>;
+  auto kern = attn_pair_kernel<T, SPLIT, TABLE, CHUNKS>;
+  constexpr uint32_t smem_bytes = CHUNKS ? SMEM2C_BYTES : SMEM2_BYTES;
   // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
   // per thread; any other count could leave the increase waiting for registers.
   static int regs = -1;
@@ -1484,7 +1677,7 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   static bool smem_set[kMaxAttnDevices] = {false};  // the attribute is per device: set it once on each
   const int dev = current_device();
   if (dev < 0 || !smem_set[dev]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM2_BYTES);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes);
     if (dev >= 0) smem_set[dev] = true;
   }
   const long long qrows = BM / s.group, mtiles = (s.rows + qrows - 1) / qrows;
@@ -1492,8 +1685,20 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
   const long long items = (long long)s.batch * s.kv_heads * pairs;
   long long ctas = sm_count();
   if (g_attention_ctas > 0 && g_attention_ctas < ctas) ctas = g_attention_ctas;
-  const long long grid = items < ctas ? items : ctas;
-  kern<<<(unsigned)grid, kThreads2, SMEM2_BYTES, stream>>>(mk, mv, mq, s, kvr);
+  // with key-range chunks a launch can have more items than this count: a full grid then
+  const long long grid = CHUNKS ? ctas : (items < ctas ? items : ctas);
+  Sm100Args sa = s;
+  if (CHUNKS) {
+    static bool parts_zeroed[kMaxAttnDevices] = {false};  // the merge counters start at zero
+    if (dev >= 0 && !parts_zeroed[dev]) {
+      if (attention_reset_partials() != SPECKV_OK) return SPECKV_ECUDA;
+      parts_zeroed[dev] = true;
+    }
+    // launches that may run at the same time (on other streams) take different slots
+    static std::atomic<unsigned> next_slot{0};
+    sa.part_slot = (int)(next_slot.fetch_add(1u) % (unsigned)kPartSlots);
+  }
+  kern<<<(unsigned)grid, kThreads2, smem_bytes, stream>>>(mk, mv, mq, sa, kvr);
   return check_launch("speckv_tree_attention_bits(sm100)");
 }
 
@@ -1501,11 +1706,21 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
 
 void attention_set_ctas(int ctas) { g_attention_ctas = ctas > 0 ? ctas : 0; }
 
+void attention_set_chunks(int on) { g_attention_chunks = on ? 1 : 0; }
+
 int attention_test_hooks(long long wait_limit_ns, int withhold_q_arrival) {
   const unsigned long long lim = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : 0ull;
   cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &lim, sizeof(lim));
   if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_withhold_q_arrival, &withhold_q_arrival, sizeof(int));
   if (e != cudaSuccess) return fail(SPECKV_ECUDA, "speckv_attention_test_hooks: %s", cudaGetErrorString(e));
+  return attention_reset_partials();
+}
+
+int attention_reset_partials() {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_part_count);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(g_part_count));
+  if (e != cudaSuccess) return fail(SPECKV_ECUDA, "attention partials reset: %s", cudaGetErrorString(e));
   return SPECKV_OK;
 }
 
@@ -1564,11 +1779,13 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
     if (bf) {
       if (split) return table ? launch_pair<__nv_bfloat16, true, true>(mk, mv, mq, s, kvr, stream)
                               : launch_pair<__nv_bfloat16, true, false>(mk, mv, mq, s, kvr, stream);
+      if (g_attention_chunks && !table) return launch_pair<__nv_bfloat16, false, false, true>(mk, mv, mq, s, kvr, stream);
       return table ? launch_pair<__nv_bfloat16, false, true>(mk, mv, mq, s, kvr, stream)
                    : launch_pair<__nv_bfloat16, false, false>(mk, mv, mq, s, kvr, stream);
     }
     if (split) return table ? launch_pair<__half, true, true>(mk, mv, mq, s, kvr, stream)
                             : launch_pair<__half, true, false>(mk, mv, mq, s, kvr, stream);
+    if (g_attention_chunks && !table) return launch_pair<__half, false, false, true>(mk, mv, mq, s, kvr, stream);
     return table ? launch_pair<__half, false, true>(mk, mv, mq, s, kvr, stream)
                  : launch_pair<__half, false, false>(mk, mv, mq, s, kvr, stream);
   }

@@ -1,6 +1,7 @@
 // Library state: per-thread last-error message, the per-device error word, and
 // the version / error-query entry points of the C ABI.
 #include "common.cuh"
+#include "attention.cuh"
 
 #include <mutex>
 #include <string>
@@ -92,5 +93,7 @@ extern "C" int speckv_device_error(uint64_t* word, void* stream) {
     return speckv::fail(SPECKV_ECUDA, "speckv_device_error: %s", cudaGetErrorString(e));
   }
   *word = host;
+  // a launch that ended in an error may have left split-item merge counters behind
+  if (host != 0ull) return speckv::attention_reset_partials();
   return SPECKV_OK;
 }

@@ -11,7 +11,8 @@ Shapes follow the benchmark configurations of the path:
                      (strong scaling), max_len 8192, prefix U{512..6144}
   qwen25_14b         48 layers, 40 q / 8 KV heads, batch 16 per GPU (128 over 8 GPUs), max_len
                      16384, prefix log-uniform [128, 14000], 25% of sequences finish per step and
-                     as many new ones are admitted
+                     as many new ones are admitted; the attention splits the longest sequences'
+                     key ranges over several CTAs (key-range chunks)
 Sequences share one physical cache length (the longest prefix); shorter
 prefixes are left-padded and their padding columns hidden by the padding
 bitmap, as the reference's prefill lays them out.
@@ -55,7 +56,7 @@ WORKLOADS = {
     'qwen25_7b': Workload('qwen25_7b', 28, 256, 28, 4, 128, 'bfloat16', 8192, ('uniform', 512, 6144), 60, 6, 10,
                           ('geometric', 3.5, 7), extra={'split_batch': True}),
     'qwen25_14b': Workload('qwen25_14b', 48, 16, 40, 8, 128, 'bfloat16', 16384, ('loguniform', 128, 14000), 60, 6,
-                           10, ('geometric', 3.5, 7), finish_fraction=0.25),
+                           10, ('geometric', 3.5, 7), finish_fraction=0.25, extra={'attention_chunks': True}),
 }
 
 

@@ -129,6 +129,8 @@ def workload_config(wl, extra=None):
                        f'depth {wl.depth} top-k {wl.topk}, accepted {wl.accept}',
            'layers': wl.layers, 'batch_per_gpu': wl.batch, 'tree_rows': wl.rows,
            'l2': 'inputs larger than L2: each step streams > 4 GB of KV pools'}
+    if wl.extra.get('attention_chunks'):
+        cfg['attention_chunks'] = 'key ranges of the longest sequences split over several CTAs (row-table runs: off)'
     cfg.update(extra or {})
     return cfg
 
@@ -1018,6 +1020,7 @@ def run_rollout(args):
         _ops.set_attention_ctas(torch.cuda.get_device_properties(device).multi_processor_count -
                                 int(os.environ['NCCL_MAX_CTAS']))
     wl = workload(args)
+    _ops.set_attention_chunks(wl.extra.get('attention_chunks', False))
     st = Round(wl, device, seed=1000 + rank, row_table=args.row_table)
     counters = AcceptanceCounters(device)
     B, H, D, L = wl.batch, wl.kv_heads, wl.dim, wl.layers

@@ -453,6 +453,19 @@ int speckv_attention_launches(int64_t* tensor_core, int64_t* cuda_core);
  * collective holds while it waits for the other ranks. No reference counterpart. */
 int speckv_attention_set_ctas(int32_t ctas);
 
+/* Key-range chunks in speckv_tree_attention_bits for this process (on = 1; 0, the default,
+ * turns them off). With chunks on, a launch in which some sequence has more key tiles than a
+ * CTA's average share of the launch (sum over sequences of key tiles x items per sequence,
+ * over the grid) splits that sequence's work items into key-range chunks of about that share,
+ * run by different CTAs; each chunk stores its unnormalised output rows with their running
+ * max and sum in the library's partial buffers, and the CTA that finishes a row tile's last
+ * chunk merges them (a softmax merge in fp32) and writes the output. For batches of ragged,
+ * long sequences (a few sequences far longer than the rest), whose longest items otherwise
+ * set the launch's duration. Launches with a row table run without chunks. Up to 4 launches
+ * with chunks may run at the same time on one device (on different streams); make the first
+ * launch with chunks on each device before any stream capture. No reference counterpart. */
+int speckv_attention_set_chunks(int32_t on);
+
 /* Test hook of the tensor-core attention kernels on the current device
  * (synchronous): every bounded wait inside them gives up after wait_limit_ns
  * (0 = the default of 2 s) and records SPECKV_DERR_TIMEOUT with the wait site;

@@ -61,17 +61,47 @@ def test_qwen25_7b_attention_long_prefixes():
     assert _ops.device_error() is None
 
 
+@pytest.mark.parametrize('chunks', [False, True])
 @pytest.mark.parametrize('kv_len', [14061, 16300])
-def test_qwen25_14b_attention_near_capacity(kv_len):
+def test_qwen25_14b_attention_near_capacity(kv_len, chunks):
     """40 q / 8 KV heads (5 query heads per KV head), one sequence at kv_len columns beside
-    log-uniform shorter ones in the same left-padded cache."""
+    log-uniform shorter ones in the same left-padded cache; with key-range chunks on, the long
+    sequence's items are split over several CTAs and merged."""
     rng = np.random.RandomState(kv_len)
     batch, rows = 6, 61
     prefix = W.prefix_lengths(rng, ('loguniform', 128, 14000), batch)
     prefix[2] = kv_len - rows
     q, k, v, vis, visible = verify_layer(batch, 40, 8, prefix, rows, kv_len)
-    out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    _ops.set_attention_chunks(chunks)
+    try:
+        out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+        again = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    finally:
+        _ops.set_attention_chunks(False)
     check_slices(q, k, v, out, visible, (slice(2, 3), slice(0, 1), slice(5, 6)))
+    assert torch.equal(out, again)  # the merge counters were left ready for the next launch
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+
+
+def test_chunked_attention_ragged_batch():
+    """Key-range chunks on a batch of 16 ragged sequences (log-uniform prefixes to 14000, the
+    Qwen2.5-14B rollout's shape): every sequence's output equals the unchunked kernel's within
+    float rounding of the merge, and the longest ones match the float32 oracle."""
+    rng = np.random.RandomState(14)
+    batch, rows = 16, 61
+    prefix = W.prefix_lengths(rng, ('loguniform', 128, 14000), batch)
+    q, k, v, vis, visible = verify_layer(batch, 40, 8, prefix, rows, 14)
+    plain = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    _ops.set_attention_chunks(True)
+    try:
+        out = _ops.tree_attention_bits(q, k, v, vis.bits, vis.first_col, 128 ** -0.5)
+    finally:
+        _ops.set_attention_chunks(False)
+    err = (out.float() - plain.float()).abs()
+    assert float(err.max()) <= 2e-2 and float(err.mean()) <= 2e-3
+    order = np.argsort(-prefix)
+    check_slices(q, k, v, out, visible, tuple(slice(int(b), int(b) + 1) for b in order[:2]))
     torch.cuda.synchronize()
     assert _ops.device_error() is None
 
