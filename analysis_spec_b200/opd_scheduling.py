@@ -23,14 +23,17 @@ def schedule(path, past, eos, workspace, packet, kernels=None, opd=None):
 
 
 def schedule_commit(path, past, eos, workspace, packet, cache, positions, past_positions, pad_rows=None,
-                    owners=None, pad_live=None, kernels=None, opd=None):
+                    owners=None, pad_live=None, kernels=None, opd=None, on_launched=None):
     """``schedule`` with the round's commit enqueued on the device before the packet read-back.
 
     Right after the padded schedule is written, one launch compacts the accepted
     suffix of every layer of ``cache`` and updates positions / padding, taking
     width and extension from the device packet (``speckv_commit_round``); the GPU
     runs the commit while the host waits for the packet. The cache is then
-    cropped to ``past + width``. Same result as ``schedule`` followed by
+    cropped to ``past + width``. ``on_launched()``, when given, is called after these launches
+    and before the host waits for the packet (e.g. to enqueue the round's counter reduction,
+    which reads the packet on the device), so its host work overlaps the GPU's. Same result as
+    ``schedule`` followed by
     ``cache.commit_accepted(indices, past, extension)`` and
     ``_ops.position_update(mask, past, positions[:, :width], past_positions, ...)``
     (helper/opd_generate.py:632-650); returns ``schedule``'s tuple.
@@ -42,12 +45,12 @@ def schedule_commit(path, past, eos, workspace, packet, cache, positions, past_p
                                       past_positions=past_positions, pad_rows=pad_rows, owners=owners,
                                       pad_live=pad_live, deferred=True)
 
-    result = _schedule(path, past, eos, workspace, packet, kernels, opd, commit)
+    result = _schedule(path, past, eos, workspace, packet, kernels, opd, commit, on_launched)
     cache.crop(past + result[5])
     return result
 
 
-def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
+def _schedule(path, past, eos, workspace, packet, kernels, opd, commit, on_launched=None):
     b, capacity = path.tokens.shape
     plugin = kernels if kernels is not None else _default_kernels
     if kernels is not None and opd is not None:
@@ -75,6 +78,8 @@ def _schedule(path, past, eos, workspace, packet, kernels, opd, commit):
     plugin.pad_schedule(path, past, eos, tokens, indices, mask, last, out_packet, snapshot=snapshot)
     if launch is not None:
         launch()
+    if on_launched is not None:
+        on_launched()
     # whole rows of the packet buffer: one contiguous copy, no gather kernel before the D2H
     host = packet[:b].cpu() if packet.is_contiguous() else packet[:b, :capacity + 4].cpu()
     if reflex:

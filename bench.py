@@ -306,9 +306,10 @@ class Round:
         return float(sum(4 * hq * rows * (int(p) + rows) * d for p in self.prefix)) * self.wl.layers
 
 
-def verify_round(st, i, marks=None):
+def verify_round(st, i, marks=None, on_launched=None):
     """One verify round; returns (width, extension, rows). `marks` gets CUDA events between phases:
-    0 visibility 1 append 2 attention 3 trace + schedule + device commit + packet read-back 4."""
+    0 visibility 1 append 2 attention 3 trace + schedule + device commit + packet read-back 4.
+    `on_launched` runs once the round's kernels are queued, before the packet read-back."""
     from analysis_spec_b200 import _ops, tree_kernels
     from analysis_spec_b200.opd_scheduling import schedule_commit
     from analysis_spec_b200.tree_verification import trace_verified_path
@@ -334,7 +335,7 @@ def verify_round(st, i, marks=None):
     path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
     rows, _, _, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
                                               st.past_positions, pad_rows=st.pad_commit, owners=st.owners,
-                                              kernels=tree_kernels)
+                                              kernels=tree_kernels, on_launched=on_launched)
     mark(4)
     live = [r for r in rows if r[1] == 0]
     extension = min(r[2] for r in live) if live else width
@@ -413,18 +414,21 @@ def run_ours(args):
 
     round_rows = []  # the host packet rows of every round, summed after the timed region as a check
 
-    def reduce_counters(rows):
-        # increments computed on the device from the packet; the all_reduce runs on a side stream
+    def enqueue_counters():
+        # increments computed on the device from the packet, the all_reduce on a side stream;
+        # queued before the host waits for the packet, so this host work overlaps the GPU's
         counters.add_device_round(st.packet, wl.batch, wl.nodes)
+
+    def reduce_counters(rows):
         round_rows.append(rows)
 
     for i in range(args.warmup):
-        _, _, rows = verify_round(st, i)
+        _, _, rows = verify_round(st, i, on_launched=enqueue_counters)
         reduce_counters(rows)
     torch.cuda.synchronize()
     if not args.no_graph:  # after the warm-up rounds: every first-call set-up has happened
         st.attn_graph = capture_attention(st)
-        _, _, rows = verify_round(st, args.warmup)  # one more warm-up round through the graph
+        _, _, rows = verify_round(st, args.warmup, on_launched=enqueue_counters)  # a warm-up round through the graph
         reduce_counters(rows)
         torch.cuda.synchronize()
     if world > 1:
@@ -440,7 +444,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     start.record()
     for i in range(args.steps):
-        w, e, rows = verify_round(st, i, ev[i])
+        w, e, rows = verify_round(st, i, ev[i], on_launched=enqueue_counters)
         reduce_counters(rows)
         widths.append((w, e))
     end.record()
@@ -1034,8 +1038,7 @@ def run_rollout(args):
     cols = st.pad.shape[1]
 
     def step(i, ev):
-        w, e, rows = verify_round(st, i)
-        counters.add_device_round(st.packet, B, wl.nodes)
+        w, e, rows = verify_round(st, i, on_launched=lambda: counters.add_device_round(st.packet, B, wl.nodes))
         commit = st.append_bytes + st.compact_bytes(w, e)
         finished = [False] * B
         for j in rng.choice(B, size=k_new, replace=False):
