@@ -27,6 +27,8 @@ _pp = ctypes.POINTER(ctypes.c_void_p)
 SIGNATURES = {
     'speckv_append_rows': [_pp, _pp, _pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _i32, _p,
                            _i64, _p],
+    'speckv_append_commit_rows': [_pp, _pp, _pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _pi64, _i32,
+                                  _p, _i64, _i64, _i64, _i64, _i64, _p],
     'speckv_compact_suffix': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i32,
                               _p, _i64, _p],
     'speckv_commit_round': [_pp, _pp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64,
@@ -64,7 +66,7 @@ SIGNATURES = {
 }
 
 # entries with a prepare / launch split (speckv_<name>_prepare + speckv_plan_launch)
-PREPARED = ('speckv_append_rows', 'speckv_commit_round')
+PREPARED = ('speckv_append_rows', 'speckv_commit_round', 'speckv_append_commit_rows')
 
 _lock = threading.Lock()
 _lib = None

@@ -79,13 +79,15 @@ def _row_table(fn, row_table, batch, pool_rows):
 
 
 @_on_device
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None):
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None, commit=None):
     """pool[l][:B, :, length:length+q] = src[l] for every layer l (one launch per 64 layers);
     with `row_table` sequence b goes to pool row row_table[b].
 
-    With ``launch=False`` the arguments are validated and marshalled now and a callable
-    that issues the launches is returned, so the host work can run while the GPU is
-    still busy with earlier launches."""
+    ``commit = (chosen, past, extension, width)`` folds the previous round's accepted-suffix
+    compaction (rows chosen[:, extension:width] to past + extension .. past + width) into the
+    same launch (speckv_append_commit_rows; without a row table). With ``launch=False`` the
+    arguments are validated and marshalled now and a callable that issues the launches is
+    returned, so the host work can run while the GPU is still busy with earlier launches."""
     k0, v0 = key_srcs[0], value_srcs[0]
     _require_cuda(key_pools[0], k0)
     bcap, heads, capacity, dim = _pool_geometry(key_pools[0])
@@ -105,6 +107,30 @@ def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=Tru
     vs = _lib.i64_array(v0.stride()[:3])
     es = key_pools[0].element_size()
     stream = _stream(k0)
+    if commit is not None:
+        chosen, past, extension, width = commit
+        if row_table is not None:
+            raise ValueError('the fused append + compaction takes no row table')
+        nvec = dim * es // 16
+        if (width - extension) * nvec > 256 or -(-rows * nvec // 128) > 32 or len(key_pools) > 64:
+            # outside the fused kernel's register stage: the compaction, then the append
+            append = append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=False)
+
+            def both():
+                if width > extension:
+                    compact_suffix(key_pools, value_pools, batch, capacity, chosen, past, extension, width)
+                append()
+            return both() if launch else both
+        if width > extension:
+            _require_cuda(chosen)
+            if chosen.dtype != torch.long or chosen.dim() != 2 or chosen.shape[0] < batch or chosen.shape[1] < width:
+                raise ValueError('chosen indices must be a (batch, >= width) int64 tensor')
+        cptr, csb, csw = (_ptr(chosen), chosen.stride(0), chosen.stride(1)) if width > extension else (None, 0, 0)
+        calls = [(_lib.ptr_array([p.data_ptr() for p in key_pools]), _lib.ptr_array([p.data_ptr() for p in value_pools]),
+                  _lib.ptr_array([s.data_ptr() for s in key_srcs]), _lib.ptr_array([s.data_ptr() for s in value_srcs]),
+                  len(key_pools), batch, heads, rows, dim, capacity, length, ks, vs, es, cptr, csb, csw, int(past),
+                  int(extension), int(width), stream)]
+        return _issue('speckv_append_commit_rows', calls, launch)
     calls = [(_lib.ptr_array([p.data_ptr() for p in key_pools[a:b]]),
               _lib.ptr_array([p.data_ptr() for p in value_pools[a:b]]),
               _lib.ptr_array([s.data_ptr() for s in key_srcs[a:b]]),

@@ -448,6 +448,84 @@ __global__ void __launch_bounds__(kThreads) commit_round_kernel(PoolTable pools,
 }
 
 // ---------------------------------------------------------------------------
+// append fused with the previous round's compaction: a round's new rows are appended in the
+// same launch that moves the previous round's accepted rows chosen[b][j], j in [ext, width),
+// to past + j. The compaction only has to land before the next attention reads the cache, so
+// it rides on the bandwidth-bound append instead of a latency-bound launch of its own. One
+// CTA per (layer, K/V, sequence, head) group reads every row it moves (the accepted rows and
+// the new rows) into registers, then stores the compacted rows, then the new rows: the new
+// rows may overwrite the old tree rows the accepted ones came from, and where the two
+// destinations overlap (a cache cropped back below past + width) the new rows win.
+// ---------------------------------------------------------------------------
+constexpr int kFoldThreads = 128;
+constexpr int kFoldMaxC = 2;  // compaction vectors per thread
+struct FoldGeom {
+  AppendGeom a;             // the append; a.dst_t0 = its first position
+  FastDiv bh;               // batch * heads
+  const int64_t* chosen;    // (batch, >= width) cache positions of the previous round's paths
+  long long csb, csw;       // chosen strides (elements)
+  long long past;           // the previous round's past: slot j goes to past + j
+  long long capacity;       // accepted positions must lie in [0, capacity)
+  int ext, width;           // slots [ext, width) move
+  unsigned long long* err;
+};
+
+template <int V, int MAXA>
+__global__ void __launch_bounds__(kFoldThreads) append_commit_kernel(PoolTable dst, SrcTable src, FoldGeom g) {
+  typedef typename Vec<V>::T T;
+  uint32_t tensor, bh, b, h;
+  g.bh.divmod(blockIdx.x, tensor, bh);
+  g.a.heads.divmod(bh, b, h);
+  const int kv = tensor & 1;
+  char* __restrict__ base = dst.ptr[tensor] + (long long)b * g.a.dst_sb + (long long)h * g.a.dst_sh;
+  const char* __restrict__ sbase = src.ptr[tensor] + (long long)b * g.a.src_sb[kv] + (long long)h * g.a.src_sh[kv];
+  const uint32_t nvec = g.a.nvec.d;
+  // accepted rows of the previous round
+  T cbuf[kFoldMaxC];
+  long long cdst[kFoldMaxC];
+  const uint32_t nc = (uint32_t)(g.width - g.ext) * nvec;
+#pragma unroll
+  for (int u = 0; u < kFoldMaxC; ++u) {
+    const uint32_t i = threadIdx.x + u * kFoldThreads;
+    cdst[u] = -1;
+    if (i < nc) {
+      uint32_t j, lv;
+      g.a.nvec.divmod(i, j, lv);
+      j += g.ext;
+      const long long pos = g.chosen[(long long)b * g.csb + (long long)j * g.csw];
+      if (pos >= 0 && pos < g.capacity) {
+        cbuf[u] = load_vec<V>(base + pos * g.a.row_bytes + (long long)lv * V);
+        cdst[u] = (g.past + j) * g.a.row_bytes + (long long)lv * V;
+      } else if (lv == 0) {
+        record_error(g.err, SPECKV_DERR_COMPACT_INDEX, pos);
+      }
+    }
+  }
+  // this round's new rows
+  T abuf[MAXA];
+  const uint32_t na = g.a.rows.d * nvec;
+#pragma unroll
+  for (int u = 0; u < MAXA; ++u) {
+    const uint32_t i = threadIdx.x + u * kFoldThreads;
+    if (i < na) {
+      uint32_t t, lv;
+      g.a.nvec.divmod(i, t, lv);
+      abuf[u] = load_vec<V>(sbase + (long long)t * g.a.src_st[kv] + (long long)lv * V);
+    }
+  }
+  __syncthreads();  // every row of the group is read before any is written
+#pragma unroll
+  for (int u = 0; u < kFoldMaxC; ++u)
+    if (cdst[u] >= 0) store_vec<V>(base + cdst[u], cbuf[u]);
+  __syncthreads();  // the new rows land last
+#pragma unroll
+  for (int u = 0; u < MAXA; ++u) {
+    const uint32_t i = threadIdx.x + u * kFoldThreads;
+    if (i < na) store_vec<V>(base + g.a.dst_t0 + (long long)i * V, abuf[u]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host helpers
 // ---------------------------------------------------------------------------
 int check_common(const char* fn, void* const* kp, void* const* vp, int32_t layers, int64_t heads,
@@ -522,11 +600,35 @@ struct CommitPlan final : LaunchPlan {
   }
 };
 
+struct FoldPlan final : LaunchPlan {
+  PoolTable dst;
+  SrcTable src;
+  FoldGeom g;
+  int vec, maxa;
+  unsigned grid;
+  int launch(cudaStream_t s) const override {
+    if (maxa == 8) {
+      SPECKV_DISPATCH_VEC(vec, append_commit_kernel<V, 8><<<grid, kFoldThreads, 0, s>>>(dst, src, g));
+    } else if (maxa == 16) {
+      SPECKV_DISPATCH_VEC(vec, append_commit_kernel<V, 16><<<grid, kFoldThreads, 0, s>>>(dst, src, g));
+    } else {
+      SPECKV_DISPATCH_VEC(vec, append_commit_kernel<V, 32><<<grid, kFoldThreads, 0, s>>>(dst, src, g));
+    }
+    return check_launch("speckv_append_commit_rows");
+  }
+};
+
 int prepare_append(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
                    const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads, int64_t rows,
                    int64_t dim, int64_t capacity, int64_t length, const int64_t* key_src_strides,
                    const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* row_table,
                    int64_t pool_rows, LaunchPlan** out);
+int prepare_fold(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
+                 const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                 int64_t dim, int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                 const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* chosen,
+                 int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, int64_t extension, int64_t width,
+                 LaunchPlan** out);
 int prepare_commit(void* const* key_pools, void* const* value_pools, int32_t layers, int64_t batch, int64_t heads,
                    int64_t dim, int64_t capacity, int64_t length, int32_t elem_bytes, const int64_t* chosen,
                    int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, const int64_t* packet,
@@ -587,6 +689,37 @@ extern "C" int speckv_append_rows_prepare(void* const* key_pools, void* const* v
   return st;
 }
 
+extern "C" int speckv_append_commit_rows(void* const* key_pools, void* const* value_pools,
+                                         const void* const* key_srcs, const void* const* value_srcs,
+                                         int32_t layers, int64_t batch, int64_t heads, int64_t rows, int64_t dim,
+                                         int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                                         const int64_t* value_src_strides, int32_t elem_bytes,
+                                         const int64_t* chosen, int64_t chosen_stride_b, int64_t chosen_stride_w,
+                                         int64_t past, int64_t extension, int64_t width, void* stream) {
+  LaunchPlan* plan = nullptr;
+  const int st = prepare_fold(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
+                              capacity, length, key_src_strides, value_src_strides, elem_bytes, chosen,
+                              chosen_stride_b, chosen_stride_w, past, extension, width, &plan);
+  return launch_once(st, plan, stream);
+}
+
+extern "C" int speckv_append_commit_rows_prepare(void* const* key_pools, void* const* value_pools,
+                                                 const void* const* key_srcs, const void* const* value_srcs,
+                                                 int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                                                 int64_t dim, int64_t capacity, int64_t length,
+                                                 const int64_t* key_src_strides, const int64_t* value_src_strides,
+                                                 int32_t elem_bytes, const int64_t* chosen, int64_t chosen_stride_b,
+                                                 int64_t chosen_stride_w, int64_t past, int64_t extension,
+                                                 int64_t width, void** plan) {
+  if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_append_commit_rows_prepare: null plan");
+  LaunchPlan* p = nullptr;
+  const int st = prepare_fold(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim,
+                              capacity, length, key_src_strides, value_src_strides, elem_bytes, chosen,
+                              chosen_stride_b, chosen_stride_w, past, extension, width, &p);
+  *plan = st ? nullptr : p;
+  return st;
+}
+
 extern "C" int speckv_plan_launch(const void* plan, void* stream) {
   if (plan == nullptr) return fail(SPECKV_EINVAL, "speckv_plan_launch: null plan");
   const LaunchPlan* p = static_cast<const LaunchPlan*>(plan);
@@ -601,6 +734,75 @@ extern "C" void speckv_plan_release(void* plan) { delete static_cast<LaunchPlan*
 
 namespace speckv {
 namespace {
+int prepare_fold(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
+                         const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads, int64_t rows,
+                         int64_t dim, int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                         const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* chosen,
+                         int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, int64_t extension,
+                         int64_t width, LaunchPlan** out) {
+  const char* fn = "speckv_append_commit_rows";
+  if (extension < 0 || width < extension || past < 0 || past + width > capacity)
+    return fail(SPECKV_EINVAL, "%s: extension %lld / width %lld / past %lld do not fit capacity %lld", fn,
+                (long long)extension, (long long)width, (long long)past, (long long)capacity);
+  if (width > extension && chosen == nullptr) return fail(SPECKV_EINVAL, "%s: null chosen", fn);
+  LaunchPlan* ap = nullptr;
+  int st = prepare_append(key_pools, value_pools, key_srcs, value_srcs, layers, batch, heads, rows, dim, capacity,
+                          length, key_src_strides, value_src_strides, elem_bytes, nullptr, 0, &ap);
+  if (st) return st;
+  AppendPlan* app = dynamic_cast<AppendPlan*>(ap);
+  if (app == nullptr) {  // nothing to append
+    if (batch == 0 || width == extension) {
+      *out = ap;
+      return SPECKV_OK;
+    }
+    delete ap;
+    return fail(SPECKV_ENOSUPPORT, "%s: no rows to append; use speckv_compact_suffix", fn);
+  }
+  const long long nvec = app->g.nvec.d;
+  const long long maxa = (rows * nvec + kFoldThreads - 1) / kFoldThreads;
+  if ((width - extension) * nvec > (long long)kFoldThreads * kFoldMaxC || maxa > 32) {
+    delete ap;
+    return fail(SPECKV_ENOSUPPORT, "%s: %lld accepted and %lld new rows of %lld vectors exceed the register "
+                "stage; use speckv_compact_suffix then speckv_append_rows", fn, (long long)(width - extension),
+                (long long)rows, nvec);
+  }
+  st = check_current_device(fn, {chosen});
+  if (st) {
+    delete ap;
+    return st;
+  }
+  unsigned long long* err = device_error_word();
+  if (err == nullptr) {
+    delete ap;
+    return fail(SPECKV_ECUDA, "%s: device error word unavailable", fn);
+  }
+  const long long groups = 2ll * layers * batch * heads;
+  if (!fits_u31(groups)) {
+    delete ap;
+    return fail(SPECKV_ENOSUPPORT, "%s: too many groups", fn);
+  }
+  FoldPlan* plan = new FoldPlan();
+  plan->device = app->device;
+  plan->dst = app->dst;
+  plan->src = app->src;
+  plan->vec = app->vec;
+  plan->g.a = app->g;
+  plan->g.bh = FastDiv((uint32_t)(batch * heads));
+  plan->g.chosen = chosen;
+  plan->g.csb = chosen_stride_b;
+  plan->g.csw = chosen_stride_w;
+  plan->g.past = past;
+  plan->g.capacity = capacity;
+  plan->g.ext = (int)extension;
+  plan->g.width = (int)width;
+  plan->g.err = err;
+  plan->maxa = maxa <= 8 ? 8 : (maxa <= 16 ? 16 : 32);
+  plan->grid = (unsigned)groups;
+  delete ap;
+  *out = plan;
+  return SPECKV_OK;
+}
+
 int prepare_append(void* const* key_pools, void* const* value_pools, const void* const* key_srcs,
                            const void* const* value_srcs, int32_t layers, int64_t batch, int64_t heads,
                            int64_t rows, int64_t dim, int64_t capacity, int64_t length,

@@ -23,27 +23,31 @@ def schedule(path, past, eos, workspace, packet, kernels=None, opd=None):
 
 
 def schedule_commit(path, past, eos, workspace, packet, cache, positions, past_positions, pad_rows=None,
-                    owners=None, pad_live=None, kernels=None, opd=None, on_launched=None):
+                    owners=None, pad_live=None, kernels=None, opd=None, on_launched=None, compact=True):
     """``schedule`` with the round's commit enqueued on the device before the packet read-back.
 
     Right after the padded schedule is written, one launch compacts the accepted
     suffix of every layer of ``cache`` and updates positions / padding, taking
     width and extension from the device packet (``speckv_commit_round``); the GPU
     runs the commit while the host waits for the packet. The cache is then
-    cropped to ``past + width``. ``on_launched()``, when given, is called after these launches
-    and before the host waits for the packet (e.g. to enqueue the round's counter reduction,
-    which reads the packet on the device), so its host work overlaps the GPU's. Same result as
-    ``schedule`` followed by
+    cropped to ``past + width``. Same result as ``schedule`` followed by
     ``cache.commit_accepted(indices, past, extension)`` and
     ``_ops.position_update(mask, past, positions[:, :width], past_positions, ...)``
     (helper/opd_generate.py:632-650); returns ``schedule``'s tuple.
+
+    ``on_launched()``, when given, is called after these launches and before the host
+    waits for the packet (e.g. to enqueue the round's counter reduction, which reads the
+    packet on the device), so its host work overlaps the GPU's. With ``compact=False``
+    the launch updates positions / padding only and the compaction is the caller's: fold
+    it into the next round's append, ``cache.update_layers(..., commit=(indices, past,
+    extension, width))``, before the next attention reads the cache.
     """
     def commit(tokens, indices, mask, out_packet):
         # prepared before the schedule kernel is launched and issued right after it, so the
         # host work of the commit overlaps the schedule kernel
         return cache.commit_scheduled(indices, past, out_packet, newly_padded=mask, positions=positions,
                                       past_positions=past_positions, pad_rows=pad_rows, owners=owners,
-                                      pad_live=pad_live, deferred=True)
+                                      pad_live=pad_live, deferred=True, compact=compact)
 
     result = _schedule(path, past, eos, workspace, packet, kernels, opd, commit, on_launched)
     cache.crop(past + result[5])

@@ -526,7 +526,7 @@ class OPDStaticCache(Cache):
         for layer in layers:
             layer.batch_size = start + count
 
-    def update_layers(self, key_states, value_states, deferred=False):
+    def update_layers(self, key_states, value_states, deferred=False, commit=None):
         """Appends key_states[l] / value_states[l] to layer l for every l in one launch.
 
         Same result as calling ``update(key_states[l], value_states[l], l)`` for each
@@ -534,6 +534,11 @@ class OPDStaticCache(Cache):
         checks, growth and argument marshalling happen now and a callable is returned
         that issues the launch and returns the views; call it before any other change
         to this cache (it lets a caller overlap this host work with a running kernel).
+
+        ``commit = (chosen, past, extension, width)``: the previous round's accepted-suffix
+        compaction, left out of its commit (``commit_scheduled(..., compact=False)``), is
+        done by the same launch before the new rows land (speckv_append_commit_rows): the
+        same cache as ``compact_suffix_inplace`` on every layer followed by this append.
         """
         if len(key_states) != len(value_states):
             raise ValueError('one key and one value tensor per layer required')
@@ -542,10 +547,12 @@ class OPDStaticCache(Cache):
             prepared.append(self._layer(idx)._prepare_append(k, v))
         layers = self.layers[:len(prepared)]
         table = layers[0]._table() if layers else None
+        if commit is not None and (table is not None or not _uniform(layers)):
+            raise ValueError('a folded commit needs uniform, table-free layers')
         if _uniform(layers):
             launches = [_ops.append_rows([l.key_pool for l in layers], [l.value_pool for l in layers],
                                          [p[0] for p in prepared], [p[1] for p in prepared], layers[0].length,
-                                         launch=False, row_table=table)]
+                                         launch=False, row_table=table, commit=commit)]
         else:
             launches = [_ops.append_rows([layer.key_pool], [layer.value_pool], [k], [v], layer.length, launch=False,
                                          row_table=table)
@@ -581,7 +588,7 @@ class OPDStaticCache(Cache):
         self.crop(past + width)
 
     def commit_scheduled(self, chosen, past, packet, newly_padded=None, positions=None, past_positions=None,
-                         pad_rows=None, owners=None, pad_live=None, deferred=False):
+                         pad_rows=None, owners=None, pad_live=None, deferred=False, compact=True):
         """``commit_accepted`` with width and extension read from the device packet.
 
         ``chosen`` (and the position operands) are the full-width schedule
@@ -589,9 +596,11 @@ class OPDStaticCache(Cache):
         enqueued before the packet is read back. The caller crops the cache to
         ``past + width`` once it knows the width. With ``deferred=True`` the
         launch is prepared now (the operands' contents may still be written by
-        kernels enqueued later) and a callable that issues it is returned.
+        kernels enqueued later) and a callable that issues it is returned. With
+        ``compact=False`` only positions / padding are updated: the compaction is then
+        the caller's, e.g. folded into the next round's ``update_layers(commit=...)``.
         """
-        layers = [l for l in self.layers if l.key_pool is not None]
+        layers = [l for l in self.layers if l.key_pool is not None] if compact else []
         pos = dict(newly_padded=newly_padded, positions=positions, past_positions=past_positions,
                    pad_rows=pad_rows, owners=owners, pad_live=pad_live)
         if not layers:

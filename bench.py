@@ -68,6 +68,9 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--layers', type=int, default=None, help='override the layer count (small profiling cases)')
     p.add_argument('--batch', type=int, default=None, help='override the per-GPU batch (small profiling cases)')
+    p.add_argument('--fold', action='store_true',
+                   help='fold each round\'s compaction into the next round\'s append launch '
+                        '(speckv_append_commit_rows); the round\'s commit launch then updates positions only')
     p.add_argument('--no-graph', action='store_true',
                    help="launch the round's attention layer by layer instead of replaying its CUDA graph")
     p.add_argument('--side-only', action='store_true',
@@ -318,7 +321,13 @@ def verify_round(st, i, marks=None, on_launched=None):
         if marks is not None:
             marks[k].record()
 
-    append = st.cache.update_layers(st.keys, st.values, deferred=True)  # host work ahead of the launches
+    # with st.fold the previous round's compaction rides on this append (its commit updated
+    # positions only); st.folded records the (width, extension) whose compaction this append does
+    fold = getattr(st, 'fold', False)
+    pending = getattr(st, 'pending_commit', None) if fold else None
+    st.folded = pending[4] if pending is not None else None
+    append = st.cache.update_layers(st.keys, st.values, deferred=True,  # host work ahead of the launches
+                                    commit=pending[:4] if pending is not None else None)
     mark(0)
     vis = st.tree.visibility(st.past, st.pad, workspace=st.vis_ws)
     mark(1)
@@ -333,12 +342,14 @@ def verify_round(st, i, marks=None, on_launched=None):
                                      row_table=getattr(k, '_speckv_rows', None))  # row-table caches only
     mark(3)
     path = trace_verified_path(st.tree, st.samples[i % len(st.samples)], EOS, workspace=st.path_ws)
-    rows, _, _, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
-                                              st.past_positions, pad_rows=st.pad_commit, owners=st.owners,
-                                              kernels=tree_kernels, on_launched=on_launched)
+    rows, _, idx, _, _, width = schedule_commit(path, st.past, EOS, st.pad_ws, st.packet, st.cache, st.positions,
+                                                st.past_positions, pad_rows=st.pad_commit, owners=st.owners,
+                                                kernels=tree_kernels, on_launched=on_launched, compact=not fold)
     mark(4)
     live = [r for r in rows if r[1] == 0]
     extension = min(r[2] for r in live) if live else width
+    if fold:
+        st.pending_commit = (idx, st.past, extension, width, (width, extension))
     st.cache.crop(st.past)  # stationary workload: the next round verifies at the same length
     return width, extension, rows
 
@@ -409,6 +420,7 @@ def run_ours(args):
                                 int(os.environ['NCCL_MAX_CTAS']))
     wl = workload(args)
     st = Round(wl, device, seed=1000 + rank)
+    st.fold = args.fold
     counters = AcceptanceCounters(device)
     st.counters = counters
 
@@ -446,7 +458,7 @@ def run_ours(args):
     for i in range(args.steps):
         w, e, rows = verify_round(st, i, ev[i], on_launched=enqueue_counters)
         reduce_counters(rows)
-        widths.append((w, e))
+        widths.append(st.folded if st.fold else (w, e))  # the compaction this step's launches did
     end.record()
     torch.cuda.synchronize()
     _lib.profile.enabled = False
@@ -468,7 +480,8 @@ def run_ours(args):
     total_ms = start.elapsed_time(end)
     # KV commit = the append launch + the device-scheduled commit launch of every step, each timed by
     # CUDA events recorded around the launch on the launching stream
-    commit_ms = sum(kernel_ms['speckv_append_rows']) + sum(kernel_ms['speckv_commit_round'])
+    append_name = 'speckv_append_commit_rows' if st.fold else 'speckv_append_rows'
+    commit_ms = sum(kernel_ms[append_name]) + sum(kernel_ms['speckv_commit_round'])
     region_ms = sum(ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps))
     verify_ms = sum(ev[i][0].elapsed_time(ev[i][1]) + ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
     attn_ms = sum(ev[i][2].elapsed_time(ev[i][3]) for i in range(args.steps))
@@ -493,8 +506,10 @@ def run_ours(args):
     history = measure_history(st) if rank == 0 else None
     release = measure_release(st) if rank == 0 else None
     hbm, tflops, peak_kind = peaks()
-    append_ms = float(np.mean(kernel_ms['speckv_append_rows']))
-    append_gbs = st.append_bytes / (append_ms * 1e-3) / 1e9
+    append_ms = float(np.mean(kernel_ms[append_name]))
+    # bytes of one launch of that kernel: the append, plus the folded compaction's on average
+    append_launch_bytes = st.append_bytes + (np.mean([st.compact_bytes(w, e) for w, e in widths]) if st.fold else 0)
+    append_gbs = append_launch_bytes / (append_ms * 1e-3) / 1e9
     if args.no_graph:
         attn_launch_ms = float(np.mean(kernel_ms['speckv_tree_attention_bits']))
     else:  # the graph region holds the layers' launches back to back: its device time / layers
@@ -503,7 +518,7 @@ def run_ours(args):
     attn_tflops = st.attention_flops() / wl.layers / (attn_launch_ms * 1e-3) / 1e12
     value = job_commit_bytes / (commit_ms * 1e-3) / 1e9
     attn_traffic = dram_traffic('speckv_tree_attention_bits', wl.layers, wl.name)
-    append_traffic = dram_traffic('speckv_append_rows', wl.layers, wl.name)
+    append_traffic = dram_traffic(append_name, wl.layers, wl.name)
     result = {
         'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s', 'n_gpus': world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 4), 'higher_is_better': True,
@@ -514,7 +529,10 @@ def run_ours(args):
         'kv_commit': {'gbs': round(value, 2), 'frac_hbm': round(value / world / hbm, 4), 'peak_gbs': hbm,
                       'ms_per_step': round(commit_ms / args.steps, 4),
                       'bytes_per_step_per_gpu': commit_bytes // args.steps,
-                      'launches': ['speckv_append_rows', 'speckv_commit_round'],
+                      'launches': [append_name, 'speckv_commit_round'],
+                      'compaction': ('folded into the next round\'s append launch; the round\'s own commit launch '
+                                     'updates positions / padding only') if st.fold else
+                                    'in the round\'s commit launch',
                       'append_region_ms_per_step': round(region_ms / args.steps, 4)},
         'tree_verify': {'steps_per_s': round(world * args.steps / (verify_ms * 1e-3), 3),
                         'ms_per_step': round(verify_ms / args.steps, 4),
@@ -523,10 +541,10 @@ def run_ours(args):
                                      'unit': 'TFLOP/s', 'frac': round(attn_tflops / tflops, 4),
                                      'traffic': attn_traffic[0], 'traffic_source': attn_traffic[1],
                                      'peak_kind': peak_kind}},
-        'roofline': {'bound': 'hbm', 'kernel': 'speckv_append_rows (all layers)', 'achieved': round(append_gbs, 1),
+        'roofline': {'bound': 'hbm', 'kernel': f'{append_name} (all layers)', 'achieved': round(append_gbs, 1),
                      'peak': hbm, 'unit': 'GB/s', 'frac': round(append_gbs / hbm, 4),
                      'traffic': append_traffic[0], 'traffic_source': append_traffic[1],
-                     'peak_kind': peak_kind, 'bytes_per_launch': st.append_bytes},
+                     'peak_kind': peak_kind, 'bytes_per_launch': int(append_launch_bytes)},
         'kernel_ms': {k: round(float(np.mean(v)), 5) for k, v in kernel_ms.items()},
         'step_phases_ms': {'visibility': round(phases[0], 4), 'append': round(phases[1], 4),
                            'attention': round(phases[2], 4), 'trace_schedule_commit_readback': round(phases[3], 4),

@@ -208,9 +208,35 @@ int speckv_history_pack(void* dst, const void* pool, int64_t pool_row_stride, in
                         int64_t row_bytes, const int64_t* offsets, int64_t rows, int64_t max_length,
                         void* stream);
 
+/* speckv_append_rows fused with the accepted-suffix compaction of the previous
+ * verify round, in one launch: for every (layer, K/V, sequence b, head h)
+ *   pool[b][h][past + j][:] = pool[b][h][chosen[b][j]][:]   for extension <= j < width
+ *   pool[b][h][length + t][:] = src[b][h][t][:]             for t < rows
+ * with every row of a (layer, K/V, sequence, head) read before any is written and
+ * the new rows written last (where the two destinations overlap, the new rows
+ * win). The compaction of a round only has to land before the next attention
+ * reads the cache, so a verify loop can move it into the next round's append
+ * (the round's own commit then updates positions only: speckv_commit_round with
+ * no layers) and run it at the append's bandwidth. chosen positions outside
+ * [0, capacity) set SPECKV_DERR_COMPACT_INDEX and are skipped. No row tables.
+ * Returns SPECKV_ENOSUPPORT when (width - extension) * row vectors exceeds 256
+ * or rows * row vectors exceeds 4096 (16-byte vectors): use
+ * speckv_compact_suffix, then speckv_append_rows. Replaces, for one round, the
+ * per-layer compact_suffix_inplace calls of helper/opd_generate.py:632-643
+ * together with the next round's StaticAppendLayer.update copies
+ * (helper/opd_static_cache.py:106-107). */
+int speckv_append_commit_rows(void* const* key_pools, void* const* value_pools,
+                              const void* const* key_srcs, const void* const* value_srcs,
+                              int32_t layers, int64_t batch, int64_t heads, int64_t rows, int64_t dim,
+                              int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                              const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* chosen,
+                              int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past, int64_t extension,
+                              int64_t width, void* stream);
+
 /* ---- Prepared launches -------------------------------------------------- */
 
-/* speckv_append_rows / speckv_commit_round split in two: *_prepare validates and
+/* speckv_append_rows / speckv_commit_round / speckv_append_commit_rows split in
+ * two: *_prepare validates and
  * packs the same arguments (without the stream) into *plan and launches nothing;
  * speckv_plan_launch enqueues the prepared kernel on `stream`, whose host cost
  * is then one kernel launch, so a caller can do the preparation while the GPU
@@ -218,6 +244,13 @@ int speckv_history_pack(void* dst, const void* pool, int64_t pool_row_stride, in
  * (the caller keeps the buffers alive and unchanged in shape); it can be
  * launched any number of times and is freed by speckv_plan_release. On error
  * *plan is NULL. Same results as the one-call entries. */
+int speckv_append_commit_rows_prepare(void* const* key_pools, void* const* value_pools,
+                                      const void* const* key_srcs, const void* const* value_srcs,
+                                      int32_t layers, int64_t batch, int64_t heads, int64_t rows, int64_t dim,
+                                      int64_t capacity, int64_t length, const int64_t* key_src_strides,
+                                      const int64_t* value_src_strides, int32_t elem_bytes, const int64_t* chosen,
+                                      int64_t chosen_stride_b, int64_t chosen_stride_w, int64_t past,
+                                      int64_t extension, int64_t width, void** plan);
 int speckv_append_rows_prepare(void* const* key_pools, void* const* value_pools,
                                const void* const* key_srcs, const void* const* value_srcs,
                                int32_t layers, int64_t batch, int64_t heads, int64_t rows,

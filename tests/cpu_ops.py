@@ -18,9 +18,13 @@ def _np(t):
     return t.numpy()
 
 
-def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None):
+def append_rows(key_pools, value_pools, key_srcs, value_srcs, length, launch=True, row_table=None, commit=None):
     assert row_table is None, 'the CPU stand-ins cover caches without a row table'
     def go():
+        if commit is not None:  # the folded compaction first (its own bounds: the pool capacity)
+            chosen, past, extension, width = commit
+            compact_suffix(key_pools, value_pools, key_srcs[0].shape[0], key_pools[0].shape[2],
+                           chosen[:, :width], past, extension, width)
         for kp, vp, ks, vs in zip(key_pools, value_pools, key_srcs, value_srcs):
             oracle.append(_np(kp), _np(vp), _np(ks), _np(vs), length)
     if launch:
