@@ -49,6 +49,8 @@ SIGNATURES = {
                                    _i64, ctypes.c_float, _i32, _p, _i64, _p],
     'speckv_tree_attention': [_p, _pi64, _p, _pi64, _p, _pi64, _p, _i32, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                               ctypes.c_float, _i32, _p],
+    'speckv_tree_attention_bits_append': [_p, _pi64, _p, _pi64, _p, _pi64, _i64, _i64, _p, _pi64, _p, _pi64, _p,
+                                          _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i32, _p],
     'speckv_device_error': [ctypes.POINTER(ctypes.c_uint64), _p],
     'speckv_plan_launch': [_p, _p],
     'speckv_causal_mask': [_p, _i32, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p],

@@ -493,6 +493,40 @@ def tree_attention_bits(query, key, value, bits, first_col, scale, out=None, row
     return out
 
 
+@_on_device
+def tree_attention_bits_append(query, key_pool, value_pool, past, key_states, value_states, bits, first_col, scale,
+                               out=None):
+    """The round's append fused into the verify attention of one layer
+    (speckv_tree_attention_bits_append): key_states / value_states ((batch, kv_heads, rows, dim)
+    views, e.g. the projection output) are stored into key_pool / value_pool ((batch, kv_heads,
+    capacity, dim)) at position `past`, and the attention runs over the past + rows positions
+    with the new rows read straight from key_states / value_states. Same pools as
+    append_rows([key_pool], [value_pool], [key_states], [value_states], past) followed by
+    tree_attention_bits over key_pool[:, :, :past + rows]; returns the output."""
+    _require_cuda(query, key_pool, value_pool, key_states, value_states, bits, first_col)
+    _check_qkv(query, key_states, value_states)
+    if key_pool.dtype != query.dtype or value_pool.dtype != query.dtype or key_pool.stride(3) != 1 or \
+            value_pool.stride(3) != 1 or tuple(key_pool.shape) != tuple(value_pool.shape) or \
+            key_pool.shape[0] != query.shape[0] or key_pool.shape[1] != key_states.shape[1] or \
+            key_pool.shape[3] != query.shape[3]:
+        raise ValueError('key/value pools must be (batch, kv_heads, capacity, head_dim) views of the query dtype')
+    batch, q_heads, rows, dim = query.shape
+    kv_heads, capacity = key_pool.shape[1], key_pool.shape[2]
+    if key_states.shape[2] != rows:
+        raise ValueError('one new key/value row per query row required')
+    if bits.dtype != torch.int32 or not bits.is_contiguous() or bits.shape[:2] != (batch, rows):
+        raise ValueError('bits must be a contiguous (batch, rows, words) int32 tensor')
+    if out is None:
+        out = torch.empty((batch, rows, q_heads, dim), device=query.device, dtype=query.dtype)
+    _lib.call('speckv_tree_attention_bits_append', query.data_ptr(), _lib.i64_array(query.stride()[:3]),
+              key_pool.data_ptr(), _lib.i64_array(key_pool.stride()[:3]), value_pool.data_ptr(),
+              _lib.i64_array(value_pool.stride()[:3]), int(past), capacity, key_states.data_ptr(),
+              _lib.i64_array(key_states.stride()[:3]), value_states.data_ptr(), _lib.i64_array(value_states.stride()[:3]),
+              bits.data_ptr(), bits.shape[2], _ptr(first_col), out.data_ptr(), batch, q_heads, kv_heads, rows, dim,
+              float(scale), _DTYPE_CODE[query.dtype], _stream(query))
+    return out
+
+
 def device_error(device=None):
     """Reads and clears the library's device error word; returns (kind, value) or None."""
     import ctypes

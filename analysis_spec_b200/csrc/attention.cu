@@ -57,6 +57,10 @@ void fill(AttnArgs& a, const void* q, const int64_t* qs, const void* k, const in
   a.first_col = nullptr;
   a.row_table = nullptr;
   a.kv_batch = batch;
+  a.past = -1;
+  a.k_new = nullptr;
+  a.v_new = nullptr;
+  for (int i = 0; i < 3; ++i) a.kns[i] = a.vns[i] = 0;
 }
 
 int launch(const char* fn, const AttnArgs& a, cudaStream_t s) {
@@ -126,6 +130,54 @@ extern "C" int speckv_tree_attention_bits(const void* q, const int64_t* q_stride
     if (!sm100_supported(a))
       return fail(SPECKV_ENOSUPPORT, "%s: row tables need the tensor-core path (head dim 128, bf16 / fp16, "
                   "16-byte aligned rows)", fn);
+  }
+  return launch(fn, a, static_cast<cudaStream_t>(stream));
+}
+
+// The round's append fused into the verify attention: the same pools and output as
+// speckv_append_rows(k_new / v_new at position past, this layer) followed by
+// speckv_tree_attention_bits over the past + rows positions, in one launch.
+extern "C" int speckv_tree_attention_bits_append(const void* q, const int64_t* q_strides,
+                                                 void* k_pool, const int64_t* k_pool_strides,
+                                                 void* v_pool, const int64_t* v_pool_strides,
+                                                 int64_t past, int64_t capacity,
+                                                 const void* k_new, const int64_t* k_new_strides,
+                                                 const void* v_new, const int64_t* v_new_strides,
+                                                 const uint32_t* bits, int64_t row_words, const int32_t* first_col,
+                                                 void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                                 int64_t rows, int64_t dim, float scale, int32_t dtype,
+                                                 void* stream) {
+  const char* fn = "speckv_tree_attention_bits_append";
+  if (past < 0 || rows < 0 || capacity < 0 || past > capacity - rows)
+    return fail(SPECKV_EINVAL, "%s: past %lld + rows %lld exceed the pools' %lld positions", fn, (long long)past,
+                (long long)rows, (long long)capacity);
+  int st = check(fn, q, q_strides, k_pool, k_pool_strides, v_pool, v_pool_strides, out, batch, q_heads, kv_heads,
+                 rows, past + rows, dim);
+  if (st || batch == 0 || rows == 0) return st;
+  if (k_new == nullptr || v_new == nullptr || k_new_strides == nullptr || v_new_strides == nullptr)
+    return fail(SPECKV_EINVAL, "%s: null new rows", fn);
+  if (bits == nullptr) return fail(SPECKV_EINVAL, "%s: null visibility bits", fn);
+  const int64_t kv_len = past + rows;
+  if (row_words < 4 * ((kv_len + 127) / 128))
+    return fail(SPECKV_EINVAL, "%s: row_words %lld below 4 * ceil(kv_len / 128)", fn, (long long)row_words);
+  if (dim != 128 || (dtype != SPECKV_BF16 && dtype != SPECKV_F16))
+    return fail(SPECKV_ENOSUPPORT, "%s: head dim 128 in bf16 / fp16 only", fn);
+  if (rows > 128)
+    return fail(SPECKV_ENOSUPPORT, "%s: %lld new rows (one 128-key tile at most)", fn, (long long)rows);
+  st = check_current_device(fn, {k_new, v_new, v_pool});
+  if (st) return st;
+  AttnArgs a;
+  fill(a, q, q_strides, k_pool, k_pool_strides, v_pool, v_pool_strides, out, batch, q_heads, kv_heads, rows, kv_len,
+       dim, scale, dtype);
+  a.bits = bits;
+  a.row_words = row_words;
+  a.first_col = first_col;
+  a.past = past;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  for (int i = 0; i < 3; ++i) {
+    a.kns[i] = k_new_strides[i];
+    a.vns[i] = v_new_strides[i];
   }
   return launch(fn, a, static_cast<cudaStream_t>(stream));
 }

@@ -21,6 +21,13 @@ struct AttnArgs {
   int dtype, mask_dtype;
   const int64_t* row_table;  // optional (bits path): pool row of each sequence's K/V
   long long kv_batch;        // rows of the K/V tensors (>= batch without a table)
+  // Fused append (bits path, past >= 0): k / v are the pools holding `past` cached positions
+  // with room for `rows` more (kv_len = past + rows); k_new / v_new, (batch, kv_heads, rows,
+  // dim) strided views, are attended as the last keys and stored into the pools at past.
+  long long past;            // < 0: no append
+  const void* k_new;
+  const void* v_new;
+  long long kns[3], vns[3];
 };
 
 // CUDA-core path (any head dim <= 256, any dtype).

@@ -113,7 +113,16 @@ struct Sm100Args {
   int batch, q_heads, kv_heads, group, rows, kv_len, mtiles;
   float scale_log2;       // softmax scale * log2(e)
   int part_slot;          // pair kernel with key-range chunks: slot of this launch's partials
+  int past;               // pair kernel with the append fused: cached positions before the tree rows
   unsigned long long* err;
+};
+
+// The append fused into the pair kernel: the round's new K / V rows ((batch, KV heads, rows,
+// 128) strided views, read as each sequence's last key tile) and the pools they are stored
+// into at position `past` (maps over the first past + rows positions, so a 128-row store box
+// writes exactly the new rows). Unused by the other instantiations.
+struct AppendMaps {
+  CUtensorMap k_new, v_new, k_pool, v_pool;
 };
 
 // K/V rows of each sequence for the pair kernel (NULL map: sequence b is row b); a separate
@@ -214,6 +223,21 @@ __device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int x, i
                "r"(x), "r"(y), "r"(z), "r"(w)
                : "memory");
 }
+
+// TMA store of one box from shared memory (bulk-group completion, no barrier); the caller
+// commits the group and waits for its reads before the shared memory is reused.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// The low n bits of a visibility word (n <= 0: none, n >= 32: all).
+__device__ __forceinline__ uint32_t low_bits(int n) { return n >= 32 ? 0xffffffffu : n <= 0 ? 0u : (1u << n) - 1u; }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -849,10 +873,19 @@ struct Item {
 // and then signals C_O_READ: the next item's first P.V waits for it.
 // TABLE: the K/V rows of sequence b come from a.row_table[b] (a separate instantiation, so
 // the table-free kernel carries no trace of it).
-template <typename T, bool SPLIT, bool TABLE, bool CHUNKS>
+// APPEND: the round's tree rows are appended by this launch. The key tiles are the cached
+// positions [0, past) in 128-key tiles (tmk / tmv cover only those positions, so the last,
+// partial tile reads zeros past them), then one tree tile [past, past + rows) loaded from
+// the new rows (am.k_new / am.v_new). The producer of the item holding row-tile pair 0 of
+// a (sequence, KV head) stores that tile into the pools at position past once it has
+// landed (TMA store from the K / V ring stage, waited for before the stage is refilled).
+// Visibility of the partial tile is cut at past; the tree tile's words start at bit past.
+template <typename T, bool SPLIT, bool TABLE, bool CHUNKS, bool APPEND = false>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                     const __grid_constant__ CUtensorMap tmq, const Sm100Args a, const KvRows kvr) {
+                     const __grid_constant__ CUtensorMap tmq, const Sm100Args a, const KvRows kvr,
+                     const __grid_constant__ AppendMaps am) {
+  static_assert(!APPEND || (!TABLE && !CHUNKS), "the fused append runs without row tables and key-range chunks");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -875,7 +908,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const int pairs = SPLIT ? 1 : (mtiles + 1) / 2;
   const int per_b = a.kv_heads * pairs;
   int n_items = a.batch * per_b;
-  const int n_tiles_all = (a.kv_len + BN - 1) / BN;
+  // APPEND: cached tiles [0, n_cached), then the tree tile n_cached
+  const int n_cached = APPEND ? (a.past + BN - 1) / BN : 0;
+  const int n_tiles_all = APPEND ? n_cached + 1 : (a.kv_len + BN - 1) / BN;
   const bool sorted = a.batch <= kMaxSortB;
   auto first_tile = [&](int b) {
     if (a.first_col == nullptr) return 0;
@@ -1025,6 +1060,28 @@ __global__ void __launch_bounds__(kThreads2, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
       const int full0 = kq ? C_K_FULL : C_V_FULL, empty0 = kq ? C_K_EMPTY : C_V_EMPTY;
       const uint32_t ring = sbase + (kq ? K2_OFF : V2_OFF);
+      // APPEND: the new rows' map and the pool map the tree tile is stored through
+      const CUtensorMap* map_new = kq ? &am.k_new : &am.v_new;
+      const CUtensorMap* map_pool = kq ? &am.k_pool : &am.v_pool;
+      if (APPEND && !qw) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map_new)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map_pool)) : "memory");
+      }
+      int pend = -1, pend_cnt = 0, pend_b = 0, pend_h = 0;  // a loaded tree tile whose store is not issued
+      bool reading[2] = {false, false};                     // a store may still read ring stage s
+      // The tree tile of load `pend_cnt` has landed (its full barrier, which the MMA warp
+      // also waits on): store it into the pools at position past. Issued one load later, so
+      // the producer does not stall on the load it has just sent.
+      auto store_tree = [&]() -> bool {
+        if (!mbar_wait(bar(full0 + pend), (pend_cnt >> 1) & 1, abort_flag, a.err, kq ? 33 : 34)) return false;
+        const uint32_t src = ring + pend * kTileBytes;
+        tma_store_4d(map_pool, src, 0, a.past, pend_h, pend_b);
+        tma_store_4d(map_pool, src + kTileHalf, 64, a.past, pend_h, pend_b);
+        bulk_commit();
+        reading[pend] = true;
+        pend = -1;
+        return true;
+      };
       int cnt = 0, issued = 0;
       int qc[2] = {0, 0};                 // Q tiles requested per row tile
       bool q_issued[2] = {false, false};  // the latest request was sent (not withheld)
@@ -1077,20 +1134,48 @@ __global__ void __launch_bounds__(kThreads2, 1)
             const int nkb = kv_row(nx.b, false);
             for (int j = nt0; j < nt0 + 2 && j < nt1; ++j)
               for (int h = 0; h < 2; ++h) {
-                tma_prefetch_4d(&tmk, h * 64, j * BN, nx.kvh, nkb);
-                tma_prefetch_4d(&tmv, h * 64, j * BN, nx.kvh, nkb);
+                if (APPEND && j == n_cached) {
+                  tma_prefetch_4d(&am.k_new, h * 64, 0, nx.kvh, nx.b);
+                  tma_prefetch_4d(&am.v_new, h * 64, 0, nx.kvh, nx.b);
+                } else {
+                  tma_prefetch_4d(&tmk, h * 64, j * BN, nx.kvh, nkb);
+                  tma_prefetch_4d(&tmv, h * 64, j * BN, nx.kvh, nkb);
+                }
               }
+          }
+          if (APPEND && pend >= 0 && !store_tree()) {
+            ok = false;
+            break;
           }
           if (cnt >= 2 && !mbar_wait(bar(empty0 + s), ((cnt >> 1) - 1) & 1, abort_flag, a.err, kq ? 21 : 22)) {
             ok = false;
             break;
           }
+          if (APPEND && reading[s]) {  // a tree-tile store still reads this stage
+            bulk_wait_read_all();
+            reading[0] = reading[1] = false;
+          }
           const uint32_t dst = ring + s * kTileBytes;
           mbar_expect_tx(bar(full0 + s), kTileBytes);
-          tma_load_4d(dst, map, bar(full0 + s), 0, i * BN, it.kvh, kb);
-          tma_load_4d(dst + kTileHalf, map, bar(full0 + s), 64, i * BN, it.kvh, kb);
+          if (APPEND && i == n_cached) {
+            tma_load_4d(dst, map_new, bar(full0 + s), 0, 0, it.kvh, it.b);
+            tma_load_4d(dst + kTileHalf, map_new, bar(full0 + s), 64, 0, it.kvh, it.b);
+            if (pair_of(it) == 0) {  // one item per (sequence, KV head) appends its rows
+              pend = s;
+              pend_cnt = cnt;
+              pend_b = it.b;
+              pend_h = it.kvh;
+            }
+          } else {
+            tma_load_4d(dst, map, bar(full0 + s), 0, i * BN, it.kvh, kb);
+            tma_load_4d(dst + kTileHalf, map, bar(full0 + s), 64, i * BN, it.kvh, kb);
+          }
           issued = cnt + 1;
         }
+      }
+      if (APPEND) {
+        if (ok && pend >= 0) store_tree();
+        bulk_wait_all();  // every store has completed before the CTA exits
       }
       // Loads still in flight must land before shared memory is released: after an abort
       // (which may come after this loop ended) nobody consumes them; in a normal run
@@ -1301,7 +1386,34 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const uint32_t* brow = a.bits + ((long long)it.b * a.rows + m.r) * a.row_words + t0 * 4;
       float m_run = -INFINITY, l_run = 0.f;
       for (int i = i_first; i < n; i += i_step) {
-        const uint4 w = m.valid ? *reinterpret_cast<const uint4*>(brow + i * 4) : make_uint4(0, 0, 0, 0);
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (!APPEND) {
+          if (m.valid) w = *reinterpret_cast<const uint4*>(brow + i * 4);
+        } else if (m.valid) {
+          // cached tile: its words, cut at past; tree tile: the words from bit past on, cut at
+          // the row count (the words are read one by one inside the row)
+          const int g = t0 + i;
+          int lim;
+          if (g < n_cached) {
+            w = *reinterpret_cast<const uint4*>(brow + i * 4);
+            lim = a.past - g * BN;
+          } else {
+            const uint32_t* rw = brow - t0 * 4;
+            const int wq = a.past >> 5, sh = a.past & 31;
+            uint32_t u[5];
+#pragma unroll
+            for (int q = 0; q < 5; ++q) u[q] = wq + q < a.row_words ? rw[wq + q] : 0u;
+            w = make_uint4(__funnelshift_r(u[0], u[1], sh), __funnelshift_r(u[1], u[2], sh),
+                           __funnelshift_r(u[2], u[3], sh), __funnelshift_r(u[3], u[4], sh));
+            lim = a.rows;
+          }
+          if (lim < BN) {
+            w.x &= low_bits(lim);
+            w.y &= low_bits(lim - 32);
+            w.z &= low_bits(lim - 64);
+            w.w &= low_bits(lim - 96);
+          }
+        }
         ok = mbar_wait(bar(C_S_FULL + t), sc & 1, abort_flag, a.err, 28);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         ++sc;
@@ -1565,7 +1677,7 @@ struct MapEntry {
   int box1, box2, dtype;
   CUtensorMap map;
 };
-constexpr int kMapCache = 256;
+constexpr int kMapCache = 512;
 
 // 4-D map with a 128-element (head dim) innermost dimension, 128-byte swizzle and a box of
 // (64, box1, box2, 1): dims[i] / strides[i] (elements) are the three outer dimensions.
@@ -1659,10 +1771,10 @@ int sm_count() {
   return n;
 }
 
-template <typename T, bool SPLIT, bool TABLE, bool CHUNKS = false>
+template <typename T, bool SPLIT, bool TABLE, bool CHUNKS = false, bool APPEND = false>
 int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Sm100Args& s,
-                const KvRows& kvr, cudaStream_t stream) {
-  auto kern = attn_pair_kernel<T, SPLIT, TABLE, CHUNKS>;
+                const KvRows& kvr, cudaStream_t stream, const AppendMaps* am = nullptr) {
+  auto kern = attn_pair_kernel<T, SPLIT, TABLE, CHUNKS, APPEND>;
   constexpr uint32_t smem_bytes = CHUNKS ? SMEM2C_BYTES : SMEM2_BYTES;
   // The setmaxnreg split assumes the block starts with exactly kRegsLaunch registers
   // per thread; any other count could leave the increase waiting for registers.
@@ -1698,8 +1810,9 @@ int launch_pair(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap&
     static std::atomic<unsigned> next_slot{0};
     sa.part_slot = (int)(next_slot.fetch_add(1u) % (unsigned)kPartSlots);
   }
-  kern<<<(unsigned)grid, kThreads2, smem_bytes, stream>>>(mk, mv, mq, sa, kvr);
-  return check_launch("speckv_tree_attention_bits(sm100)");
+  static const AppendMaps no_append{};  // the argument of the instantiations without the append
+  kern<<<(unsigned)grid, kThreads2, smem_bytes, stream>>>(mk, mv, mq, sa, kvr, am != nullptr ? *am : no_append);
+  return check_launch(APPEND ? "speckv_tree_attention_bits_append(sm100)" : "speckv_tree_attention_bits(sm100)");
 }
 
 }  // namespace
@@ -1734,14 +1847,23 @@ bool sm100_supported(const AttnArgs& a) {
   if (a.batch > (1 << 20) || a.kv_len > (1 << 30)) return false;
   // visibility words are read 16 bytes at a time
   if (a.bits != nullptr && (a.row_words % 4 != 0 || (uintptr_t)a.bits % 16 != 0)) return false;
+  if (a.past >= 0) {  // the appended rows are read by TMA as well
+    for (int i = 0; i < 3; ++i)
+      if ((a.kns[i] * 2) % 16 != 0 || (a.vns[i] * 2) % 16 != 0) return false;
+    if (((uintptr_t)a.k_new | (uintptr_t)a.v_new) % 16 != 0) return false;
+  }
   return true;
 }
 
 int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   const uint32_t* bits = a.bits;
+  const bool append = a.past >= 0;
+  // with the append fused the pools are read over the cached positions only (an empty
+  // cache still gets a valid one-position map, which no tile reads)
+  const long long load_len = append ? (a.past > 0 ? a.past : 1) : a.kv_len;
   CUtensorMap mk, mv;
-  if (!make_kv_map(&mk, a.k, a.ks, a.kv_batch, a.kv_heads, a.kv_len, a.dtype) ||
-      !make_kv_map(&mv, a.v, a.vs, a.kv_batch, a.kv_heads, a.kv_len, a.dtype))
+  if (!make_kv_map(&mk, a.k, a.ks, a.kv_batch, a.kv_heads, load_len, a.dtype) ||
+      !make_kv_map(&mv, a.v, a.vs, a.kv_batch, a.kv_heads, load_len, a.dtype))
     return fail(SPECKV_ECUDA, "speckv_tree_attention: cuTensorMapEncodeTiled failed");
   unsigned long long* err = device_error_word();
   if (err == nullptr) return fail(SPECKV_ECUDA, "speckv_tree_attention: device error word unavailable");
@@ -1764,6 +1886,8 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
   s.kv_len = (int)a.kv_len;
   s.mtiles = (int)((s.group * a.rows + BM - 1) / BM);
   s.scale_log2 = a.scale * 1.4426950408889634f;
+  s.part_slot = 0;
+  s.past = append ? (int)a.past : 0;
   s.err = err;
   const KvRows kvr{a.row_table, (int)a.kv_batch};
   const bool bf = a.dtype == SPECKV_BF16;
@@ -1776,6 +1900,18 @@ int attention_sm100(const AttnArgs& a, cudaStream_t stream) {
       return fail(SPECKV_ECUDA, "speckv_tree_attention_bits: cuTensorMapEncodeTiled failed for the query");
     // at most one 128-row tile per (sequence, KV head): the two warpgroups split the keys
     const bool split = (long long)s.group * s.rows <= BM, table = kvr.map != nullptr;
+    if (append) {
+      AppendMaps am;
+      if (!make_kv_map(&am.k_new, a.k_new, a.kns, a.batch, a.kv_heads, a.rows, a.dtype) ||
+          !make_kv_map(&am.v_new, a.v_new, a.vns, a.batch, a.kv_heads, a.rows, a.dtype) ||
+          !make_kv_map(&am.k_pool, a.k, a.ks, a.kv_batch, a.kv_heads, a.past + a.rows, a.dtype) ||
+          !make_kv_map(&am.v_pool, a.v, a.vs, a.kv_batch, a.kv_heads, a.past + a.rows, a.dtype))
+        return fail(SPECKV_ECUDA, "speckv_tree_attention_bits_append: cuTensorMapEncodeTiled failed");
+      if (bf) return split ? launch_pair<__nv_bfloat16, true, false, false, true>(mk, mv, mq, s, kvr, stream, &am)
+                           : launch_pair<__nv_bfloat16, false, false, false, true>(mk, mv, mq, s, kvr, stream, &am);
+      return split ? launch_pair<__half, true, false, false, true>(mk, mv, mq, s, kvr, stream, &am)
+                   : launch_pair<__half, false, false, false, true>(mk, mv, mq, s, kvr, stream, &am);
+    }
     if (bf) {
       if (split) return table ? launch_pair<__nv_bfloat16, true, true>(mk, mv, mq, s, kvr, stream)
                               : launch_pair<__nv_bfloat16, true, false>(mk, mv, mq, s, kvr, stream);

@@ -180,6 +180,23 @@ class StaticAppendLayer(CacheLayerMixin):
         self.length = end
         return self.keys, self.values
 
+    def update_attend(self, query, key_states, value_states, visibility, scale, out=None):
+        """``update(key_states, value_states)`` and the tree-verify attention of ``query`` over
+        the updated cache in one launch (speckv_tree_attention_bits_append): the new rows are
+        attended straight from ``key_states`` / ``value_states`` and stored into the pools by
+        the same kernel. ``visibility`` carries ``bits`` / ``first_col`` over the
+        ``length + rows`` columns (``PackedTree.visibility``); returns the attention output
+        (batch, rows, q_heads, head_dim). Table-free caches only."""
+        if self._table() is not None:
+            raise ValueError('the fused append needs a cache without a row table')
+        key_states, value_states, end = self._prepare_append(key_states, value_states)
+        rows = self.batch_size
+        out = _ops.tree_attention_bits_append(query, self.key_pool[:rows], self.value_pool[:rows], self.length,
+                                              key_states, value_states, visibility.bits, visibility.first_col, scale,
+                                              out=out)
+        self.length = end
+        return out
+
     def get_seq_length(self):
         return self.length
 
@@ -397,6 +414,11 @@ class OPDStaticCache(Cache):
 
     def update(self, key_states, value_states, layer_idx, *args, **kwargs):
         return self._layer(layer_idx).update(key_states, value_states)
+
+    def update_attend(self, query, key_states, value_states, layer_idx, visibility, scale, out=None):
+        """``update(key_states, value_states, layer_idx)`` fused with the verify attention that
+        reads the layer right after it (StaticAppendLayer.update_attend); returns its output."""
+        return self._layer(layer_idx).update_attend(query, key_states, value_states, visibility, scale, out=out)
 
     def get_seq_length(self, layer_idx=0):
         return self.layers[layer_idx].length if layer_idx < len(self.layers) else 0

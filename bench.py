@@ -324,17 +324,25 @@ def verify_round(st, i, marks=None, on_launched=None):
     # with st.fold the previous round's compaction rides on this append (its commit updated
     # positions only); st.folded records the (width, extension) whose compaction this append does
     fold = getattr(st, 'fold', False)
+    # with st.fused the append rides on the attention launches (update_attend): no append launch
+    fused = getattr(st, 'fused', False)
     pending = getattr(st, 'pending_commit', None) if fold else None
     st.folded = pending[4] if pending is not None else None
-    append = st.cache.update_layers(st.keys, st.values, deferred=True,  # host work ahead of the launches
-                                    commit=pending[:4] if pending is not None else None)
+    append = None if fused else st.cache.update_layers(st.keys, st.values, deferred=True,  # host work first
+                                                       commit=pending[:4] if pending is not None else None)
     mark(0)
     vis = st.tree.visibility(st.past, st.pad, workspace=st.vis_ws)
     mark(1)
-    views = append()
+    views = append() if append is not None else None
     mark(2)
     if getattr(st, 'attn_graph', None) is not None:
         st.attn_graph.replay()  # the same 36 launches, captured once (capture_attention)
+        if fused:  # the host half of update_attend: every layer now holds past + rows positions
+            for layer in st.cache.layers:
+                layer.length = st.past + st.wl.rows
+    elif fused:
+        for l in range(st.wl.layers):
+            st.cache.update_attend(st.queries[l], st.keys[l], st.values[l], l, vis, st.scale, out=st.out[l])
     else:
         for l in range(st.wl.layers):
             k, v = views[l]
@@ -369,8 +377,13 @@ def capture_attention(st):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         for l in range(st.wl.layers):
-            _ops.tree_attention_bits(st.queries[l], views[l][0], views[l][1], vis.bits, vis.first_col, st.scale,
-                                     out=st.out[l])
+            if getattr(st, 'fused', False):  # the append fused in: pools read up to past, new rows stored
+                _ops.tree_attention_bits_append(st.queries[l], st.cache.layers[l].key_pool[:st.wl.batch],
+                                                st.cache.layers[l].value_pool[:st.wl.batch], st.past, st.keys[l],
+                                                st.values[l], vis.bits, vis.first_col, st.scale, out=st.out[l])
+            else:
+                _ops.tree_attention_bits(st.queries[l], views[l][0], views[l][1], vis.bits, vis.first_col, st.scale,
+                                         out=st.out[l])
     torch.cuda.synchronize()
     return graph
 
@@ -501,6 +514,10 @@ def run_ours(args):
     total_ms, commit_ms, verify_ms, attn_ms, region_ms, *phases, between = times.tolist()
     job_commit_bytes = moved.item()
 
+    # the same rounds with the append fused into the attention launches (rank 0, after the line)
+    # (a rank-0-only measurement: its counters reduce nothing across ranks when the job has several)
+    fused = measure_fused(st, args.steps, args.warmup, not args.no_graph,
+                          AcceptanceCounters(device) if world == 1 else None) if rank == 0 and not st.fold else None
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
     draft = measure_draft(st) if rank == 0 else None
     history = measure_history(st) if rank == 0 else None
@@ -557,6 +574,7 @@ def run_ours(args):
         'draft_step': draft,
         'history_step': history,
         'release_step': release,
+        'fused_append': fused,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result['cpu_baseline'] = cpu_baseline(wl, budget_s=10.0)
@@ -718,6 +736,56 @@ def measure_history(st, iters=20, warmup=3, hidden=2048):
             'timing': 'device time per step (steps queued behind a GPU spin); launch_bound_us: back to back on an '
                       'idle GPU, host launch cost included',
             'bit_exact_vs_torch_sequence': bool(same)}
+
+
+def measure_fused(st, steps, warmup, graph, counters=None):
+    """The same verify rounds with each layer's append fused into its attention launch
+    (speckv_tree_attention_bits_append, through OPDStaticCache.update_attend; with `graph`
+    the 36 fused launches replay from a CUDA graph as the line's attention does): the round
+    has no append launch, the attention launches store the tree rows. Run after the line's
+    timed rounds on the same cache, with the acceptance counters of the line's rounds when
+    `counters` is given; device time from CUDA events around the round's phases."""
+    import torch
+    wl = st.wl
+    saved = st.attn_graph
+    st.fused, st.attn_graph = True, None
+
+    def enqueue():
+        counters.add_device_round(st.packet, wl.batch, wl.nodes)
+
+    hook = enqueue if counters is not None else None
+    try:
+        for i in range(warmup):
+            verify_round(st, i, on_launched=hook)
+        torch.cuda.synchronize()
+        if graph:
+            st.attn_graph = capture_attention(st)
+            verify_round(st, warmup, on_launched=hook)
+            torch.cuda.synchronize()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(steps):
+            verify_round(st, i, ev[i], on_launched=hook)
+        end.record()
+        torch.cuda.synchronize()
+    finally:
+        st.fused, st.attn_graph = False, saved
+    phases = [sum(ev[i][j].elapsed_time(ev[i][j + 1]) for i in range(steps)) / steps for j in range(4)]
+    between = (sum(ev[i][4].elapsed_time(ev[i + 1][0]) for i in range(steps - 1)) / (steps - 1)
+               if steps > 1 else 0.0)
+    per_layer_us = phases[2] / wl.layers * 1e3
+    return {'ms_per_step': round(start.elapsed_time(end) / steps, 4),
+            'verify_ms_per_step': round(phases[0] + phases[2], 4),
+            'attention_with_append_us_per_layer': round(per_layer_us, 2),
+            'attention_tflops': round(st.attention_flops() / wl.layers / (per_layer_us * 1e-6) / 1e12, 2),
+            'step_phases_ms': {'visibility': round(phases[0], 4), 'append': round(phases[1], 4),
+                               'attention_with_append': round(phases[2], 4),
+                               'trace_schedule_commit_readback': round(phases[3], 4),
+                               'between_rounds': round(between, 4)},
+            'append_launches_per_step': 0, 'kv_bytes_stored_by_attention_per_step': st.append_bytes // 2,
+            'acceptance_counters': counters is not None,
+            'launch': 'speckv_tree_attention_bits_append per layer' + (' (CUDA graph)' if graph else '')}
 
 
 def measure_release(st, fraction=0.25, spin_ms=8.0):

@@ -472,6 +472,33 @@ int speckv_tree_attention_bits(const void* q, const int64_t* q_strides,
                                int64_t rows, int64_t kv_len, int64_t dim, float scale,
                                int32_t dtype, const int64_t* row_table, int64_t kv_batch, void* stream);
 
+/* The round's tree-row append fused into the verify attention of one layer: the
+ * same pools and output as speckv_append_rows(k_new / v_new into the pools at
+ * position past) followed by speckv_tree_attention_bits over kv_len = past + rows,
+ * in one launch. Replaces, per decoder layer, the two copy_ calls of
+ * StaticAppendLayer.update (helper/opd_static_cache.py:106-107) together with the
+ * attention that reads the cache right after them (transformers
+ * integrations/sdpa_attention.py:40-104, called from helper/opd_generate.py:490).
+ * k_pool / v_pool: (batch, kv_heads, capacity, dim) strided pools holding `past`
+ * cached positions, past + rows <= capacity; k_new / v_new: (batch, kv_heads, rows,
+ * dim) strided views (the projection output). The cached positions are attended in
+ * 128-key tiles (the last one cut at past) and the new rows as one more tile read
+ * straight from k_new / v_new, which the kernel stores into the pools once loaded.
+ * Head dim 128, bf16 / fp16, rows <= 128, 16-byte aligned bases and strides; no row
+ * table. bits / row_words / first_col as for speckv_tree_attention_bits over the
+ * past + rows columns. The attention sums over a different key-tile split than
+ * speckv_tree_attention_bits, so outputs agree to rounding, not bit for bit; the
+ * pools are bit-exact. */
+int speckv_tree_attention_bits_append(const void* q, const int64_t* q_strides,
+                                      void* k_pool, const int64_t* k_pool_strides,
+                                      void* v_pool, const int64_t* v_pool_strides,
+                                      int64_t past, int64_t capacity,
+                                      const void* k_new, const int64_t* k_new_strides,
+                                      const void* v_new, const int64_t* v_new_strides,
+                                      const uint32_t* bits, int64_t row_words, const int32_t* first_col,
+                                      void* out, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                      int64_t rows, int64_t dim, float scale, int32_t dtype, void* stream);
+
 /* Launches issued since the library was loaded by speckv_tree_attention /
  * speckv_tree_attention_bits calls, per kernel family: *tensor_core the tcgen05
  * kernels, *cuda_core the CUDA-core kernel (other head dims, fp32). Replays of a
