@@ -518,6 +518,9 @@ def run_ours(args):
     # (a rank-0-only measurement: its counters reduce nothing across ranks when the job has several)
     fused = measure_fused(st, args.steps, args.warmup, not args.no_graph,
                           AcceptanceCounters(device) if world == 1 else None) if rank == 0 and not st.fold else None
+    if fused is not None:  # DRAM bytes of one fused launch, from the committed ncu capture
+        fused['traffic'], fused['traffic_source'] = dram_traffic('speckv_tree_attention_bits_append', wl.layers,
+                                                                 wl.name)
     e2e = None if args.no_e2e else measure_e2e(st, args, world)
     draft = measure_draft(st) if rank == 0 else None
     history = measure_history(st) if rank == 0 else None
