@@ -25,6 +25,9 @@ def draft_sdpa(query_states, key_states, value_states, attention_mask, num_key_v
     Hq == Hkv * num_key_value_groups. Returns (B, Hq, R, D)."""
     if dropout_p:
         raise ValueError('draft_sdpa is the rollout (inference) attention: dropout_p must be 0')
+    pending = getattr(key_states, '_speckv_pending', None)
+    if pending is not None:  # rows an OPDStaticCache(fuse_append=True) left to a verify attention
+        pending[0]._flush()
     if query_states.shape[1] != key_states.shape[1] * num_key_value_groups:
         raise ValueError(f'draft_sdpa: {query_states.shape[1]} query heads for {key_states.shape[1]} KV heads '
                          f'x {num_key_value_groups} groups')

@@ -57,6 +57,32 @@ class StaticAppendLayer(CacheLayerMixin):
         super().__init__()
         self.capacity = capacity
         self.is_initialized = False
+        # (key_states, value_states, position) of rows appended with the owner's fuse_append on
+        # and not yet in the pools: the next verify attention over this layer's views stores
+        # them (speckv_tree_attention_bits_append); any other use of the pools stores them first
+        self._pending = None
+
+    # ---- deferred append (OPDStaticCache(fuse_append=True)) ---------------------
+    def _flush(self):
+        """Stores rows whose append was deferred to the attention (one append launch)."""
+        pending, self._pending = self._pending, None
+        if pending is not None:
+            k, v, position = pending
+            _ops.append_rows([self.key_pool], [self.value_pool], [k], [v], position, row_table=self._table())
+
+    def _fusable(self, key_states, value_states):
+        """True when the rows can be left to the fused append + attention kernel: the owner
+        asked for it, no row table, head dim 128 in bf16 / fp16, at most 128 rows, CUDA views
+        whose bases and strides the kernel's tensor maps can address (16-byte units)."""
+        owner = self.owner
+        if owner is None or not owner.fuse_append or self._table() is not None:
+            return False
+        for t in (key_states, value_states):
+            if not t.is_cuda or t.dtype not in (torch.bfloat16, torch.float16) or t.dim() != 4 or \
+                    t.shape[-1] != 128 or not 1 <= t.shape[-2] <= 128 or t.stride(3) != 1 or \
+                    t.data_ptr() % 16 or any(st * t.element_size() % 16 for st in t.stride()[:3]):
+                return False
+        return True
 
     # ---- views ---------------------------------------------------------------
     @property
@@ -79,6 +105,7 @@ class StaticAppendLayer(CacheLayerMixin):
 
     @property
     def keys(self):
+        self._flush()
         return self._view(self.key_pool)
 
     @keys.setter
@@ -88,6 +115,7 @@ class StaticAppendLayer(CacheLayerMixin):
 
     @property
     def values(self):
+        self._flush()
         return self._view(self.value_pool)
 
     @values.setter
@@ -100,6 +128,7 @@ class StaticAppendLayer(CacheLayerMixin):
         # the visible length / batch); anything else would silently detach the pool.
         if pool is None:
             raise RuntimeError('cache assignment before initialization')
+        self._flush()
         if view.untyped_storage().data_ptr() != pool.untyped_storage().data_ptr():
             raise RuntimeError('use batch_select_indices for row remap; external KV replacement is unsupported')
         self.length = view.shape[-2]
@@ -136,6 +165,7 @@ class StaticAppendLayer(CacheLayerMixin):
         batch_needed = self.batch_size if batch_needed is None else batch_needed
         if needed <= self.capacity and batch_needed <= self.batch_capacity:
             return
+        self._flush()
         capacity = self._capacity_for(max(needed, 2 * self.capacity)) if needed > self.capacity else self.capacity
         rows = max(batch_needed, self.batch_capacity)
         shape = (rows, self.key_pool.shape[1], capacity, self.key_pool.shape[-1])
@@ -174,7 +204,16 @@ class StaticAppendLayer(CacheLayerMixin):
         return key_states, value_states, end
 
     def update(self, key_states, value_states, *args, **kwargs):
+        self._flush()
         key_states, value_states, end = self._prepare_append(key_states, value_states)
+        if self._fusable(key_states, value_states):
+            # the rows are stored by the verify attention that reads these views
+            # (tree_attention.tree_verify_attention); the views carry the pending append
+            self._pending = (key_states, value_states, self.length)
+            self.length = end
+            keys, values = self._view(self.key_pool), self._view(self.value_pool)
+            keys._speckv_pending = values._speckv_pending = (self, self._pending)
+            return keys, values
         _ops.append_rows([self.key_pool], [self.value_pool], [key_states], [value_states], self.length,
                          row_table=self._table())
         self.length = end
@@ -189,6 +228,7 @@ class StaticAppendLayer(CacheLayerMixin):
         (batch, rows, q_heads, head_dim). Table-free caches only."""
         if self._table() is not None:
             raise ValueError('the fused append needs a cache without a row table')
+        self._flush()
         key_states, value_states, end = self._prepare_append(key_states, value_states)
         rows = self.batch_size
         out = _ops.tree_attention_bits_append(query, self.key_pool[:rows], self.value_pool[:rows], self.length,
@@ -210,10 +250,12 @@ class StaticAppendLayer(CacheLayerMixin):
         return self.length + query_length, 0
 
     def crop(self, length):
+        self._flush()
         target = length if length >= 0 else self.length + length
         self.length = max(0, min(self.length, target))
 
     def reset(self):
+        self._pending = None
         self.length = 0
 
     # ---- remap / release -------------------------------------------------------
@@ -246,6 +288,7 @@ class StaticAppendLayer(CacheLayerMixin):
         if self._table() is not None:
             raise RuntimeError('with a row table, remap rows through the cache (OPDStaticCache.batch_select_indices)')
         new_batch = indices.numel()
+        self._flush()
         self._grow(self.length, new_batch)
         _ops.remap_rows([self.key_pool], [self.value_pool], indices, self.length, self._remap_scratch(new_batch))
         self._count_select(new_batch)
@@ -271,6 +314,7 @@ class StaticAppendLayer(CacheLayerMixin):
         if self._table() is not None:
             raise RuntimeError('with a row table, release rows through the cache (OPDStaticCache.swap_remove)')
         count = sources.numel()
+        self._flush()
         if count and self.length:
             _ops.move_rows([self.key_pool], [self.value_pool], sources, destinations, self.length)
         self._count_swap(new_batch, count)
@@ -317,12 +361,23 @@ def _uniform(layers):
 
 
 class OPDStaticCache(Cache):
-    """HF ``Cache`` whose layers are StaticAppendLayer pools kept across rollouts."""
+    """HF ``Cache`` whose layers are StaticAppendLayer pools kept across rollouts.
 
-    def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256, row_table=False):
+    ``fuse_append=True`` (no reference counterpart): ``update`` leaves a layer's new rows
+    out of the pools and tags the views it returns; the verify attention that reads them
+    (``tree_attention.tree_verify_attention``, registered as 'speckv_tree') then attends
+    the rows from the projection and stores them in the same launch
+    (speckv_tree_attention_bits_append). Every other use of the cache stores pending rows
+    first (``flush``). The flag may be switched at any time (e.g. on only for the verify
+    forward); a model whose attention is not this package's must not read views of a
+    cache with pending rows without calling ``flush()`` first.
+    """
+
+    def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256, row_table=False, fuse_append=False):
         if capacity < 1 or chunk_size < 1 or batch_capacity < 0:
             raise ValueError('positive KV capacity/chunk and nonnegative batch capacity required')
         self.uses_row_table = bool(row_table)
+        self.fuse_append = bool(fuse_append)
         # host copy of the table: a permutation of the pool rows, live sequences first
         # (entry b < batch is sequence b's row), the rows free for admission after them
         self._rows = []
@@ -375,8 +430,15 @@ class OPDStaticCache(Cache):
             return None
         return list(self._rows[:self.layers[0].batch_size])
 
+    def flush(self):
+        """Stores every layer's rows whose append was left to the attention (fuse_append)."""
+        for layer in self.layers:
+            layer._flush()
+
     # ---- rollout lifetime ------------------------------------------------------
     def begin_rollout(self, batch, batch_capacity):
+        for layer in self.layers:
+            layer._pending = None  # the lengths restart at 0: rows of the last rollout are dropped
         self.batch_capacity = max(self.batch_capacity, batch_capacity)
         self.kv_rows_moved = 0
         for layer in self.layers:
@@ -389,6 +451,7 @@ class OPDStaticCache(Cache):
 
     def end_rollout(self, max_retained_tokens=0):
         for layer in self.layers:
+            layer._pending = None
             layer.length = layer.batch_size = 0
         if max_retained_tokens and any(layer.capacity > max_retained_tokens for layer in self.layers):
             self.layers.clear()
@@ -451,6 +514,7 @@ class OPDStaticCache(Cache):
         layers = self.layers
         if not layers:
             return
+        self.flush()
         if self.uses_row_table and layers[0].key_pool is not None:
             # through the table to pool rows, written to rows [0, new_batch): the table is identity after
             indices = self._device_rows(layers[0].batch_size)[indices]
@@ -484,6 +548,7 @@ class OPDStaticCache(Cache):
         self.kv_rows_moved += indices.numel()
 
     def swap_remove(self, new_batch, sources, destinations):
+        self.flush()
         layers = self.layers
         if self.uses_row_table and layers and layers[0].key_pool is not None:
             self._swap_remove_rows(new_batch, sources, destinations)
@@ -525,6 +590,7 @@ class OPDStaticCache(Cache):
         layers = self.layers[:len(key_states)]
         if not layers or len(key_states) != len(value_states) or len(layers) != len(self.layers):
             raise ValueError('one key and one value tensor per layer required')
+        self.flush()
         count = key_states[0].shape[0]
         length = layers[0].length
         if any(l.length != length or l.batch_size != layers[0].batch_size for l in layers):
@@ -564,6 +630,7 @@ class OPDStaticCache(Cache):
         """
         if len(key_states) != len(value_states):
             raise ValueError('one key and one value tensor per layer required')
+        self.flush()
         prepared = []
         for idx, (k, v) in enumerate(zip(key_states, value_states)):
             prepared.append(self._layer(idx)._prepare_append(k, v))
@@ -596,6 +663,7 @@ class OPDStaticCache(Cache):
         ``crop(past + chosen.shape[1])`` (helper/opd_generate.py:632-643).
         """
         width = chosen.shape[1]
+        self.flush()
         layers = self.layers
         if layers and extension != width:
             table = layers[0]._table()
@@ -622,6 +690,7 @@ class OPDStaticCache(Cache):
         ``compact=False`` only positions / padding are updated: the compaction is then
         the caller's, e.g. folded into the next round's ``update_layers(commit=...)``.
         """
+        self.flush()
         layers = [l for l in self.layers if l.key_pool is not None] if compact else []
         pos = dict(newly_padded=newly_padded, positions=positions, past_positions=past_positions,
                    pad_rows=pad_rows, owners=owners, pad_live=pad_live)

@@ -51,18 +51,47 @@ def dense_mask_visibility(attention_mask, mask, batch, rows, kv_len):
     return vis
 
 
+def _pending_rows(key):
+    """(layer, (key_states, value_states, position)) when `key` is a view of an
+    OPDStaticCache(fuse_append=True) layer whose latest rows are not stored yet, else None."""
+    tag = getattr(key, '_speckv_pending', None)
+    if tag is None or tag[0]._pending is not tag[1]:
+        return None
+    return tag
+
+
+def _bits_attention(query, key, value, bits, first_col, scale, rows_table, pending):
+    """The visibility-bits kernel, with the layer's pending rows appended by the same launch
+    when the views carry them (speckv_tree_attention_bits_append), else after storing them."""
+    if pending is not None:
+        layer, (k_new, v_new, position) = pending
+        if (k_new.shape[-2] == query.shape[2] and position + k_new.shape[-2] == key.shape[-2] and
+                k_new.dtype == query.dtype and rows_table is None):
+            batch = key.shape[0]
+            out = _ops.tree_attention_bits_append(query, layer.key_pool[:batch], layer.value_pool[:batch], position,
+                                                  k_new, v_new, bits, first_col, scale)
+            layer._pending = None  # stored by that launch
+            return out
+        layer._flush()
+    return _ops.tree_attention_bits(query, key, value, bits, first_col, scale, row_table=rows_table)
+
+
 def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None, is_causal=None,
                           **kwargs):
-    """(module, q (B,Hq,R,D), k/v (B,Hkv,L,D), additive mask (B,1,R,L)) -> (out (B,R,Hq,D), None)."""
+    """(module, q (B,Hq,R,D), k/v (B,Hkv,L,D), additive mask (B,1,R,L)) -> (out (B,R,Hq,D), None).
+
+    K/V views of an ``OPDStaticCache(fuse_append=True)`` whose latest rows are still pending
+    take the fused append + attention kernel on the visibility-bits path; any other path
+    stores the rows first."""
     if dropout:
         raise ValueError('tree_verify_attention is an inference kernel (dropout must be 0)')
     scale = scaling if scaling is not None else query.shape[-1] ** -0.5
     rows_table = getattr(key, '_speckv_rows', None)  # K/V of a row-table cache: every pool row
+    pending = _pending_rows(key)
     vis = attention_mask if hasattr(attention_mask, 'first_col') else getattr(attention_mask, '_speckv_visibility',
                                                                             None)
     if vis is not None and key.shape[-2] == vis.past + vis.rows and query.shape[2] == vis.rows:
-        return _ops.tree_attention_bits(query, key, value, vis.bits, vis.first_col, scale,
-                                        row_table=rows_table), None
+        return _bits_attention(query, key, value, vis.bits, vis.first_col, scale, rows_table, pending), None
     mask = attention_mask
     if mask is not None and mask.shape[-1] > key.shape[-2]:
         mask = mask[:, :, :, :key.shape[-2]]
@@ -74,8 +103,9 @@ def tree_verify_attention(module, query, key, value, attention_mask, dropout=0.0
         batch, rows, kv_len = query.shape[0], query.shape[2], key.shape[-2]
         dense = dense_mask_visibility(attention_mask, mask, batch, rows, kv_len)
         if dense is not None:
-            return _ops.tree_attention_bits(query, key, value, dense.bits, dense.first_col, scale,
-                                            row_table=rows_table), None
+            return _bits_attention(query, key, value, dense.bits, dense.first_col, scale, rows_table, pending), None
+    if pending is not None:  # the dense-mask and CUDA-core kernels read the rows from the pools
+        pending[0]._flush()
     if rows_table is not None:
         raise ValueError('K/V of a row-table cache need a 0 / lowest-valued mask (the visibility-bits kernel), '
                          'head dim 128 and bf16 / fp16')

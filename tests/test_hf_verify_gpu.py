@@ -151,3 +151,99 @@ def test_tree_verify_forward_through_a_row_table():
     assert err.max().item() <= 2e-2 * max(scale, 1.0), (err.max().item(), scale)
     assert err.mean().item() <= 2e-3 * max(scale, 1.0), (err.mean().item(), scale)
     assert (logits.argmax(-1) == ref.argmax(-1)).float().mean().item() >= 0.95
+
+
+@pytest.mark.parametrize('attach_bits', [True, False])
+def test_fused_append_on_the_verify_forward(attach_bits):
+    """OPDStaticCache(fuse_append=True) on the real model's verify forward: each decoder layer's
+    update leaves its tree rows to the registered attention, which appends them in its own
+    launch (speckv_tree_attention_bits_append; no append launch in the forward). Against the
+    same forward on a cache without the flag: pools bit-exact, logits within bf16 tolerance,
+    identical greedy acceptance; with the dense mask alone (no bits attached) the mask's
+    one-time conversion feeds the fused kernel too. The first layer's pools are compared
+    bit for bit; deeper layers' tree rows come from hidden states that went through the
+    previous layer's attention, whose output agrees to rounding only (the fused kernel splits
+    the key tiles differently), so those rows are compared within bf16 tolerance."""
+    from analysis_spec_b200 import _lib
+    name = register()
+    model = _model()
+    ids, mask2d, parents, tokens, positions = _inputs()
+    pad_np = np.zeros((B, PROMPT + ROWS), dtype=bool)
+    pad_np[:, :PROMPT] = mask2d == 0
+    pad = torch.from_numpy(pad_np).cuda()
+    tree = PackedTree(torch.from_numpy(parents).cuda(), torch.from_numpy(tokens).cuda(),
+                      torch.zeros(B, ROWS, dtype=torch.long, device='cuda'), DEPTH)
+    results, pools, calls = {}, {}, {}
+    for fuse in (False, True):
+        model.config._attn_implementation = 'sdpa'  # both prefills through transformers' SDPA
+        for layer in model.model.layers:
+            layer.self_attn.config._attn_implementation = 'sdpa'
+        cache = _prefill(model, ids, mask2d)  # the flag goes on after the prefill
+        cache.fuse_append = fuse
+        mask = tree.attention_mask(PROMPT, torch.bfloat16, pad)
+        if attach_bits:
+            mask = tree.visibility(PROMPT, pad).attach(mask)
+        _lib.profile.reset()
+        _lib.profile.enabled = True
+        try:
+            results[fuse] = _verify(model, cache, tree, tokens, positions, mask, name)
+        finally:
+            _lib.profile.enabled = False
+        calls[fuse] = {k: len(v) for k, v in _lib.profile.events.items()}
+        assert cache.get_seq_length() == PROMPT + ROWS
+        assert all(layer._pending is None for layer in cache.layers)
+        pools[fuse] = [(l.key_pool[:B, :, :PROMPT + ROWS].clone(), l.value_pool[:B, :, :PROMPT + ROWS].clone())
+                       for l in cache.layers]
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+    layers = len(model.model.layers)
+    assert calls[True].get('speckv_tree_attention_bits_append') == layers, calls[True]
+    assert 'speckv_append_rows' not in calls[True] and calls[False].get('speckv_append_rows') == layers, calls
+    for i, ((k0, v0), (k1, v1)) in enumerate(zip(pools[False], pools[True])):
+        end = PROMPT + ROWS if i == 0 else PROMPT
+        for a, b in ((k0, k1), (v0, v1)):
+            assert torch.equal(a[:, :, :end].view(torch.int16), b[:, :, :end].view(torch.int16)), i
+            tail = (a[:, :, PROMPT:].float() - b[:, :, PROMPT:].float()).abs()
+            assert tail.max().item() <= 2e-2 * max(a.float().abs().max().item(), 1.0), (i, tail.max().item())
+    ref = results[False]
+    scale = ref.abs().max().item()
+    err = (results[True] - ref).abs()
+    assert err.max().item() <= 2e-2 * max(scale, 1.0), (err.max().item(), scale)
+    assert err.mean().item() <= 2e-3 * max(scale, 1.0), (err.mean().item(), scale)
+    eos = VOCAB + 1
+    lengths = {}
+    for fuse, logits in results.items():
+        path = trace_verified_path(tree, logits.argmax(-1), eos)
+        rows, *_ = schedule(path, PROMPT, eos, None, None, tree_kernels)
+        lengths[fuse] = [r[0] for r in rows]
+    assert lengths[True] == lengths[False], lengths
+
+
+def test_fused_append_rows_are_stored_before_other_uses():
+    """Rows a fuse_append cache left pending are in the pools before anything else reads or
+    moves them: a read of the keys / values views, and a remap of the batch."""
+    torch.manual_seed(1)
+    batch, heads, past, rows = 3, 2, 40, 7
+    base = [(0.5 * torch.randn(batch, heads, past, 128, device='cuda')).bfloat16() for _ in range(2)]
+    new = [(0.5 * torch.randn(batch, heads, rows, 128, device='cuda')).bfloat16() for _ in range(2)]
+    ref = OPDStaticCache(64, batch_capacity=batch)
+    ref.update(base[0], base[1], 0)
+    keys_ref, values_ref = ref.update(new[0], new[1], 0)
+    cache = OPDStaticCache(64, batch_capacity=batch, fuse_append=True)
+    cache.update(base[0], base[1], 0)
+    cache.update(new[0], new[1], 0)
+    layer = cache.layers[0]
+    assert layer._pending is not None  # left to the attention
+    keys = layer.keys  # a public read stores them
+    assert layer._pending is None
+    assert torch.equal(keys.view(torch.int16), keys_ref.view(torch.int16))
+    cache.update(new[1], new[0], 0)
+    assert cache.layers[0]._pending is not None
+    idx = torch.tensor([2, 0, 1], device='cuda')
+    cache.batch_select_indices(idx)  # a remap stores them first
+    ref.update(new[1], new[0], 0)
+    ref.batch_select_indices(idx)
+    torch.cuda.synchronize()
+    assert torch.equal(cache.layers[0].keys.view(torch.int16), ref.layers[0].keys.view(torch.int16))
+    assert torch.equal(cache.layers[0].values.view(torch.int16), ref.layers[0].values.view(torch.int16))
+    assert _ops.device_error() is None
