@@ -79,7 +79,7 @@ def _tree_rows_before(calls, i):
 class Replay:
     """Decodes recorded arguments into this package's objects and checks every result."""
 
-    def __init__(self, z, meta, device='cuda'):
+    def __init__(self, z, meta, device='cuda', fused=False):
         from analysis_spec_b200 import opd_attention, opd_history, opd_scheduling, opd_static_cache
         from analysis_spec_b200 import tree_attention, tree_verification
         self.z, self.meta, self.device = z, meta, torch.device(device)
@@ -89,6 +89,11 @@ class Replay:
         self.attention = []  # (layer, max err, mean err)
         self.schedules = []
         self.statistics = {}
+        # fused: the loop's caches run with fuse_append on, so each target layer's update is
+        # stored by the attention call after it; results that read a layer with rows still
+        # pending (the update's returned views, the state check) are checked after that call
+        self.fused = fused
+        self.deferred = []
 
     # ---- decoding ---------------------------------------------------------------------
     def view(self, x):
@@ -103,6 +108,10 @@ class Replay:
             return array(self.z, x, self.device)
         if 'view' in x:
             v = self.view(x)
+            layer = self.objects[x['view']].layers[x['layer']]
+            if self.fused and layer._pending is not None:
+                v._speckv_pending = (layer, layer._pending)  # as the views update returned
+                return v
             assert sha(v) == x['sha'], f'input view {x["view"]} layer {x["layer"]} differs before the call'
             return v
         if 'empty' in x:
@@ -195,6 +204,8 @@ class Replay:
                     assert (layer.length, layer.batch_size, list(layer.key_pool.shape)) == (n, b, shape), \
                         f'{where}: {name} layer {l} (length, batch, pool) = ' \
                         f'{(layer.length, layer.batch_size, tuple(layer.key_pool.shape))} vs {(n, b, shape)}'
+                    if layer._pending is not None:  # fused: checked once the attention stored them
+                        continue
                     assert sha(layer.key_pool[:b, :, :n]) == ksha, f'{where}: {name} layer {l} K rows differ'
                     assert sha(layer.value_pool[:b, :, :n]) == vsha, f'{where}: {name} layer {l} V rows differ'
                 assert obj.kv_rows_moved == st['kv_rows_moved'], f'{where}: {name} kv_rows_moved'
@@ -205,6 +216,7 @@ class Replay:
     # ---- calls ------------------------------------------------------------------------
     def call(self, i, c):
         fn, where = c['fn'], f'call {i} {c["fn"]}'
+        self.settle()
         if fn == 'attention':
             return self.attention_call(c, where)
         cls, _, method = fn.partition('.')
@@ -222,6 +234,8 @@ class Replay:
             out = target(*args, **kwargs)
             if 'created' in c:
                 self.objects[c['created']] = out
+                if self.fused and isinstance(out, self.osc.OPDStaticCache):
+                    out.fuse_append = True
             if fn == 'opd_scheduling.schedule':
                 self.schedules.append(out[0])
             exp = c['out']
@@ -229,7 +243,12 @@ class Replay:
                 self.statistics[c['args'][0]['object']] = dict(out)
                 exp = {'dict': [[k, v] for k, v in exp['dict'] if k != SCRATCH_STAT]}
                 out = {k: v for k, v in out.items() if k != SCRATCH_STAT}
-            self.match(exp, out, where)
+            layer = (self.objects[c['args'][0]['object']].layers[c['args'][3]]
+                     if fn == 'OPDStaticCache.update' else None)
+            if layer is not None and layer._pending is not None:
+                self.deferred.append((layer, exp, out, where))
+            else:
+                self.match(exp, out, where)
         self.check_state(c['state'], where)
         if fn == 'opd_scheduling.compact_suffix_inplace':
             # the loop then stores the returned views back into the layer (_cache_set_layer,
@@ -255,10 +274,28 @@ class Replay:
             f'{where}: attention max {float(err.max()):.3g} mean {float(err.mean()):.3g}'
         self.check_state(c['state'], where)
 
+    def settle(self):
+        """Checks the views an update returned with its rows still pending, before the next
+        call changes anything: their contents as the loop sees them are the pools' rows with
+        the pending rows in place (copies; the cache itself is not touched, so the next call
+        still has to store or fuse them, which the state check after it verifies)."""
+        for layer, exp, got, at in self.deferred:
+            token = layer._pending
+            assert token is not None, f'{at}: pending rows stored before the next call'
+            k_new, v_new, position = token
+            items = exp['tuple']
+            assert len(items) == 2 and len(got) == 2, at
+            for e, view, rows in zip(items, got, (k_new, v_new)):
+                assert list(view.shape) == e['shape'] and list(view.stride()) == e['stride'], at
+                logical = view.clone()
+                logical[:, :, position:position + rows.shape[-2]] = rows
+                assert sha(logical) == e['sha'], f'{at}: K/V bytes differ'
+        self.deferred = []
 
-def replay(path=TRACE):
+
+def replay(path=TRACE, fused=False):
     z, meta = load_trace(path)
-    r = Replay(z, meta)
+    r = Replay(z, meta, fused=fused)
     for i, c in enumerate(meta['calls']):
         r.call(i, c)
     torch.cuda.synchronize()
