@@ -750,7 +750,7 @@ def measure_fused(st, steps, warmup, graph, counters=None):
     `counters` is given; device time from CUDA events around the round's phases."""
     import torch
     wl = st.wl
-    saved = st.attn_graph
+    saved = getattr(st, "attn_graph", None)
     st.fused, st.attn_graph = True, None
 
     def enqueue():

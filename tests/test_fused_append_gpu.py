@@ -206,3 +206,34 @@ def test_fused_append_refusals():
         _ops.tree_attention_bits_append(big[0], big[1], big[2], 10, big[3], big[4], big[5].bits, big[5].first_col,
                                         0.1)
     assert _ops.device_error() is None
+
+
+def test_fused_append_bounded_wait_runs_out_and_unwinds():
+    """A bounded wait of the fused kernel made to run out (test hooks: a 2 ms limit, CTA 0's
+    first Q tile withheld): the launch reports 'wait timeout' and returns, every tree-row store
+    it issued has completed, and the context stays usable: the next call on restored pools
+    appends and attends exactly as before the failure."""
+    q, kpool, vpool, knew, vnew, vis, _ = case(16, 16, 2, 61, 1400, seed=31)
+    scale = 128 ** -0.5
+    k0, v0 = kpool.clone(), vpool.clone()
+    ref = _ops.tree_attention_bits_append(q, kpool, vpool, 1400, knew, vnew, vis.bits, vis.first_col, scale)
+    kref, vref = kpool.clone(), vpool.clone()
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+    kpool.copy_(k0)
+    vpool.copy_(v0)
+    try:
+        _lib.call('speckv_attention_test_hooks', 2_000_000, 1)
+        _ops.tree_attention_bits_append(q, kpool, vpool, 1400, knew, vnew, vis.bits, vis.first_col, scale)
+        torch.cuda.synchronize()
+        err = _ops.device_error()
+    finally:
+        _lib.call('speckv_attention_test_hooks', 0, 0)
+    assert err is not None and err[0] == 'wait timeout', err
+    kpool.copy_(k0)
+    vpool.copy_(v0)
+    again = _ops.tree_attention_bits_append(q, kpool, vpool, 1400, knew, vnew, vis.bits, vis.first_col, scale)
+    torch.cuda.synchronize()
+    assert _ops.device_error() is None
+    assert torch.equal(again.view(torch.int16), ref.view(torch.int16))
+    assert same_bits(kpool, kref) and same_bits(vpool, vref)
