@@ -370,7 +370,10 @@ class OPDStaticCache(Cache):
     (speckv_tree_attention_bits_append). Every other use of the cache stores pending rows
     first (``flush``). The flag may be switched at any time (e.g. on only for the verify
     forward); a model whose attention is not this package's must not read views of a
-    cache with pending rows without calling ``flush()`` first.
+    cache with pending rows without calling ``flush()`` first. Until they are stored the
+    cache holds references to the ``key_states`` / ``value_states`` given to ``update``:
+    they must not be modified in place before the attention (or ``flush``) runs, and it
+    should run on the stream that produced them.
     """
 
     def __init__(self, capacity=256, *, batch_capacity=0, chunk_size=256, row_table=False, fuse_append=False):
