@@ -35,3 +35,87 @@ def test_product_kernels_refuse_cpu_tensors(monkeypatch):
                          [torch.zeros(1, 1, 1, 2)], 0)
     with pytest.raises(RuntimeError, match='need CUDA tensors'):
         cache_mod.OPDStaticCache(8).update(torch.zeros(1, 1, 1, 2), torch.zeros(1, 1, 1, 2), 0)
+
+
+def _fused_pair(monkeypatch, layers=2, batch=3, heads=2, past=10):
+    """A fuse_append cache and a plain one holding the same prefix; on CPU the rows a fused
+    update leaves pending are stored by whichever cache operation comes next."""
+    import torch
+    monkeypatch.setattr(cache_mod.StaticAppendLayer, '_fusable',
+                        lambda self, k, v: self.owner is not None and self.owner.fuse_append)
+    torch.manual_seed(0)
+    fused = cache_mod.OPDStaticCache(16, batch_capacity=batch, chunk_size=16, fuse_append=True)
+    plain = cache_mod.OPDStaticCache(16, batch_capacity=batch, chunk_size=16)
+    for l in range(layers):
+        k, v = torch.randn(batch, heads, past, 8).bfloat16(), torch.randn(batch, heads, past, 8).bfloat16()
+        fused.update(k, v, l)
+        plain.update(k, v, l)
+    return fused, plain
+
+
+def _same(fused, plain):
+    import torch
+    assert [l.length for l in fused.layers] == [l.length for l in plain.layers]
+    assert [l.batch_size for l in fused.layers] == [l.batch_size for l in plain.layers]
+    for a, b in zip(fused.layers, plain.layers):
+        assert a._pending is None
+        assert torch.equal(a.keys.view(torch.int16), b.keys.view(torch.int16))
+        assert torch.equal(a.values.view(torch.int16), b.values.view(torch.int16))
+
+
+def _new_rows(layers=2, batch=3, heads=2, rows=4):
+    import torch
+    return [(torch.randn(batch, heads, rows, 8).bfloat16(), torch.randn(batch, heads, rows, 8).bfloat16())
+            for _ in range(layers)]
+
+
+@pytest.mark.parametrize('then', ['read', 'update', 'crop', 'select', 'repeat', 'swap_remove', 'commit',
+                                  'update_layers', 'grow'])
+def test_fused_append_rows_are_stored_before_the_next_operation(monkeypatch, then):
+    """OPDStaticCache(fuse_append=True): an update returns views with its rows still pending
+    (left to the verify attention); every other cache operation stores them first, so the
+    cache ends as a plain cache given the same calls."""
+    import torch
+    fused, plain = _fused_pair(monkeypatch)
+    rows = _new_rows()
+    for c in (fused, plain):
+        for l, (k, v) in enumerate(rows):
+            keys, values = c.update(k, v, l)
+            assert keys.shape[-2] == 14
+    assert all(l._pending is not None for l in fused.layers)
+    # only the views update returned carry the pending rows
+    assert getattr(fused.layers[0]._view(fused.layers[0].key_pool), '_speckv_pending', None) is None
+    more = _new_rows(rows=3)
+    big = _new_rows(rows=5)
+    for c in (fused, plain):
+        if then == 'read':
+            _ = [(l.keys, l.values) for l in c.layers]
+        elif then == 'update':
+            for l, (k, v) in enumerate(more):
+                c.update(k, v, l)
+        elif then == 'crop':
+            c.crop(12)
+        elif then == 'select':
+            c.batch_select_indices(torch.tensor([2, 0]))
+        elif then == 'repeat':
+            c.batch_repeat_interleave(2)
+        elif then == 'swap_remove':
+            c.swap_remove(2, torch.tensor([2]), torch.tensor([0]))
+        elif then == 'commit':
+            chosen = torch.tensor([[10, 12, 13], [10, 11, 13], [10, 13, 12]])
+            c.commit_accepted(chosen, 10, 1)
+        elif then == 'update_layers':
+            c.update_layers([k for k, _ in more], [v for _, v in more])
+        elif then == 'grow':  # an append past the capacity copies the history into new pools
+            for l, (k, v) in enumerate(big):
+                c.update(k, v, l)
+    fused.flush()  # rows a final fused update left pending (update / grow) are stored now
+    _same(fused, plain)
+
+
+def test_fused_append_pending_rows_are_dropped_by_reset(monkeypatch):
+    fused, plain = _fused_pair(monkeypatch)
+    for l, (k, v) in enumerate(_new_rows()):
+        fused.update(k, v, l)
+    fused.begin_rollout(3, 3)
+    assert all(l._pending is None and l.length == 0 for l in fused.layers)
