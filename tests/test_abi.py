@@ -105,3 +105,23 @@ def test_attention_counters_and_hook_arguments(lib):
         _lib.call('speckv_attention_test_hooks', -1, 0)
     with pytest.raises(_lib.SpecKVError, match='0 / 1 switch'):
         _lib.call('speckv_attention_test_hooks', 0, 2)
+
+
+def test_fused_append_attention_refuses_before_any_launch(lib):
+    """speckv_tree_attention_bits_append checks sizes on the host: rows beyond the pools'
+    capacity, visibility rows too short for past + rows columns, another head dim, a tree
+    wider than one 128-key tile. The pointers are never dereferenced."""
+    s = _lib.i64_array([0, 0, 0])
+    p = 16
+
+    def call(past, capacity, rows, dim, row_words):
+        _lib.call('speckv_tree_attention_bits_append', p, s, p, s, p, s, past, capacity, p, s, p, s, p, row_words,
+                  None, p, 1, 16, 2, rows, dim, 1.0, _lib.BF16, None)
+    with pytest.raises(_lib.SpecKVError, match='exceed'):
+        call(100, 120, 61, 128, 8)
+    with pytest.raises(_lib.SpecKVError, match='row_words'):
+        call(300, 400, 61, 128, 4)
+    with pytest.raises(_lib.SpecKVError, match='head dim 128'):
+        call(10, 400, 61, 64, 4)
+    with pytest.raises(_lib.SpecKVError, match='128-key tile'):
+        call(10, 400, 129, 128, 8)
