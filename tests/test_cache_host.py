@@ -119,3 +119,35 @@ def test_fused_append_pending_rows_are_dropped_by_reset(monkeypatch):
         fused.update(k, v, l)
     fused.begin_rollout(3, 3)
     assert all(l._pending is None and l.length == 0 for l in fused.layers)
+
+
+def test_verify_attention_takes_the_fused_kernel_only_for_matching_pending_rows(monkeypatch):
+    """tree_verify_attention's choice for views of a fuse_append cache (kernels stubbed): pending
+    rows that are exactly the query's tree rows go to speckv_tree_attention_bits_append (and are
+    then no longer pending); any other shape stores them first and runs the bits kernel."""
+    import torch
+    from types import SimpleNamespace
+    from analysis_spec_b200 import tree_attention
+    calls = []
+    stub = SimpleNamespace(
+        tree_attention_bits_append=lambda q, kp, vp, past, k, v, bits, first, scale, out=None: calls.append(
+            ('fused', past, k.shape[-2])) or torch.zeros(q.shape[0], q.shape[2], q.shape[1], q.shape[3]),
+        tree_attention_bits=lambda q, k, v, bits, first, scale, row_table=None: calls.append(
+            ('bits', k.shape[-2])) or torch.zeros(q.shape[0], q.shape[2], q.shape[1], q.shape[3]))
+    monkeypatch.setattr(tree_attention, '_ops', stub)
+    fused, _ = _fused_pair(monkeypatch)
+    rows = _new_rows(rows=4)
+    module = SimpleNamespace(is_causal=True, training=False)
+    vis = SimpleNamespace(bits=None, first_col=None, past=10, rows=4)
+    for l, (k, v) in enumerate(rows):
+        keys, values = fused.update(k, v, l)
+        q = torch.zeros(3, 4, 4, 8).bfloat16()
+        tree_attention.tree_verify_attention(module, q, keys, values, vis)
+        assert fused.layers[l]._pending is None
+    assert calls == [('fused', 10, 4), ('fused', 10, 4)]
+    calls.clear()
+    keys, values = fused.update(*_new_rows(rows=4)[0], 0)  # pending again at position 14
+    q = torch.zeros(3, 4, 2, 8).bfloat16()  # 2 query rows for 4 pending rows: not the fused case
+    tree_attention.tree_verify_attention(module, q, keys, values, SimpleNamespace(bits=None, first_col=None,
+                                                                                  past=16, rows=2))
+    assert calls == [('bits', 18)] and fused.layers[0]._pending is None
